@@ -1,0 +1,11 @@
+"""cobra-gpu-kernel_b200: the reference's single transformer-layer forward on B200.
+
+Public API (mirrors dalberrt/COBRA-GPU-Kernel's drop-in module):
+    TransformerConfig, B200TransformerLayer, SelfAttentionWeights
+Native boundary: ``include/cobra_b200.h`` (ctypes binding in ``_lib``).
+"""
+
+from .layer import B200TransformerLayer, SelfAttentionWeights, TransformerConfig  # noqa: F401
+from . import _lib  # noqa: F401
+
+__all__ = ["B200TransformerLayer", "SelfAttentionWeights", "TransformerConfig"]

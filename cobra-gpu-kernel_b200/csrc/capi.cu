@@ -1,0 +1,461 @@
+// capi.cu -- the extern "C" boundary declared in include/cobra_b200.h.
+//
+// Validates shapes and pointers, carves the caller's workspace, builds the TMA
+// tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry
+// point, so no libcuda link is needed) and launches the kernels on the
+// caller's stream. Nothing here allocates, synchronises (except
+// b200l_read_status, which exists to do so) or keeps state other than a
+// per-device cache of kernel attributes and device properties.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_set>
+
+#include "../../include/cobra_b200.h"
+#include "attn.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "rowln.cuh"
+
+using namespace b200l;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(B200L_ERR_LAUNCH, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- device cache
+struct DevInfo {
+  int sms = 0;
+  int major = 0;
+  bool ok = false;
+};
+std::mutex g_mu;
+DevInfo g_dev[64];
+std::unordered_set<unsigned long long> g_attr_done;
+
+int device_info(DevInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B200L_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_dev[dev].ok) {
+    int sms = 0, major = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute(cc major)");
+    g_dev[dev].sms = sms;
+    g_dev[dev].major = major;
+    g_dev[dev].ok = true;
+  }
+  *out = g_dev[dev];
+  if (out->major != 10) return fail(B200L_ERR_DEVICE, "device %d has compute capability %d.x, need 10.x (sm_100a)", dev, out->major);
+  return B200L_OK;
+}
+
+// Sets the dynamic shared memory limit of a kernel once per device.
+int ensure_smem(const void* func, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const unsigned long long key = reinterpret_cast<unsigned long long>(func) * 131ull + (unsigned long long)dev;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_attr_done.count(key)) return B200L_OK;
+  }
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_attr_done.insert(key);
+  return B200L_OK;
+}
+
+// ---------------------------------------------------------------- tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// fp16 tensor of rank 2 or 3; dims/strides innermost first, strides in bytes
+// for dims 1.. ; box innermost first.
+int make_map(CUtensorMap* map, const void* base, int rank, const unsigned long long* dims,
+             const unsigned long long* strides_bytes, const unsigned* box, CUtensorMapSwizzle swz, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(B200L_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t gd[3], gs[2];
+  cuuint32_t bx[3], es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) gs[i] = strides_bytes[i];
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bx, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200L_ERR_LAUNCH, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", what, (int)r);
+  return B200L_OK;
+}
+
+int map_rows_k(CUtensorMap* map, const void* base, unsigned long long rows, int k, unsigned box_rows,
+               const char* what) {
+  const unsigned long long dims[2] = {(unsigned long long)k, rows};
+  const unsigned long long strides[1] = {(unsigned long long)k * 2};
+  const unsigned box[2] = {64, box_rows};
+  return make_map(map, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, what);
+}
+
+// ---------------------------------------------------------------- plan
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Plan {
+  int B, S, d, H, dh, dhp, sp;
+  long long T;
+  size_t off_q, off_k, off_vt, off_ctx, off_h, total;
+};
+
+int make_plan(const b200l_layer_desc* desc, Plan* p) {
+  if (!desc) return fail(B200L_ERR_NULL_POINTER, "layer descriptor is NULL");
+  const int B = desc->batch, S = desc->seq_len, d = desc->d_model, H = desc->num_heads;
+  if (B <= 0 || S <= 0 || d <= 0 || H <= 0)
+    return fail(B200L_ERR_BAD_SHAPE, "batch, seq_len, d_model and num_heads must be positive (got %d, %d, %d, %d)", B, S, d, H);
+  if (d % H != 0) return fail(B200L_ERR_BAD_SHAPE, "d_model (%d) must be divisible by num_heads (%d)", d, H);
+  const int dh = d / H;
+  if (dh % 32 != 0 || dh > 256)
+    return fail(B200L_ERR_UNSUPPORTED_HEAD_DIM, "head_dim %d unsupported: need a multiple of 32 in [32, 256]", dh);
+  if (d > 2048) return fail(B200L_ERR_BAD_SHAPE, "d_model %d > 2048 is not supported", d);
+  const long long T = (long long)B * S;
+  const int dhp = dh <= 32 ? 32 : dh <= 64 ? 64 : dh <= 128 ? 128 : 256;
+  const int sp = (S + 7) / 8 * 8;
+  if ((long long)B * H * ((S + 127) / 128) > 0x7fffffffLL || T > 0x7fffffffLL)
+    return fail(B200L_ERR_BAD_SHAPE, "problem too large for 32-bit tile indices");
+  p->B = B; p->S = S; p->d = d; p->H = H; p->dh = dh; p->dhp = dhp; p->sp = sp; p->T = T;
+  size_t off = 1024;  // status block (256 B) padded to keep every region 1024-aligned
+  const size_t qk = (size_t)B * H * S * dhp * 2;
+  p->off_q = off; off = align_up(off + qk, 1024);
+  p->off_k = off; off = align_up(off + qk, 1024);
+  p->off_vt = off; off = align_up(off + (size_t)B * H * dhp * sp * 2, 1024);
+  p->off_ctx = off; off = align_up(off + (size_t)T * d * 2, 1024);
+  p->off_h = off;
+  if (d > 256) off = align_up(off + (size_t)T * d * 2, 1024);
+  p->total = off;
+  return B200L_OK;
+}
+
+int check_common(const b200l_layer_desc* desc, const void* ws, size_t ws_bytes, Plan* p, DevInfo* dev) {
+  int rc = make_plan(desc, p);
+  if (rc) return rc;
+  if ((rc = device_info(dev))) return rc;
+  if (!ws) return fail(B200L_ERR_NULL_POINTER, "workspace is NULL");
+  if (reinterpret_cast<uintptr_t>(ws) % 1024) return fail(B200L_ERR_ALIGNMENT, "workspace must be 1024-byte aligned");
+  if (ws_bytes < p->total)
+    return fail(B200L_ERR_WORKSPACE_TOO_SMALL, "workspace has %zu bytes, need %zu", ws_bytes, p->total);
+  const void* ptrs[] = {desc->wqkv, desc->bqkv, desc->wo, desc->bo, desc->ln1_w, desc->ln1_b, desc->ln2_w, desc->ln2_b};
+  const char* names[] = {"wqkv", "bqkv", "wo", "bo", "ln1_w", "ln1_b", "ln2_w", "ln2_b"};
+  for (int i = 0; i < 8; ++i) {
+    if (!ptrs[i]) return fail(B200L_ERR_NULL_POINTER, "%s is NULL", names[i]);
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16) return fail(B200L_ERR_ALIGNMENT, "%s must be 16-byte aligned", names[i]);
+  }
+  return B200L_OK;
+}
+
+QkvOut qkv_out(const Plan& p, void* ws) {
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  QkvOut o;
+  o.q = reinterpret_cast<__half*>(w + p.off_q);
+  o.k = reinterpret_cast<__half*>(w + p.off_k);
+  o.vt = reinterpret_cast<__half*>(w + p.off_vt);
+  o.S = p.S; o.H = p.H; o.dh = p.dh; o.dhp = p.dhp; o.sp = p.sp; o.d = p.d;
+  return o;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return B200L_OK;
+}
+
+// ---------------------------------------------------------------- launches
+template <int VPL, bool F16>
+int launch_row_ln_t(const float* in, void* out, const float* w, const float* b, float eps, long long T, int d,
+                    cudaStream_t st) {
+  const long long blocks = (T + 7) / 8;
+  row_ln_kernel<VPL, F16><<<(unsigned)blocks, 256, 0, st>>>(in, out, w, b, eps, T, d);
+  return check_launch("row_ln_kernel");
+}
+template <bool F16>
+int launch_row_ln(const float* in, void* out, const float* w, const float* b, float eps, long long T, int d,
+                  cudaStream_t st) {
+  const int v = (d + 127) / 128;
+  if (v <= 1) return launch_row_ln_t<1, F16>(in, out, w, b, eps, T, d, st);
+  if (v <= 2) return launch_row_ln_t<2, F16>(in, out, w, b, eps, T, d, st);
+  if (v <= 4) return launch_row_ln_t<4, F16>(in, out, w, b, eps, T, d, st);
+  if (v <= 8) return launch_row_ln_t<8, F16>(in, out, w, b, eps, T, d, st);
+  return launch_row_ln_t<16, F16>(in, out, w, b, eps, T, d, st);
+}
+
+template <int KP>
+int launch_qkv_lnfused_t(const b200l_layer_desc* desc, const Plan& p, const float* x, void* ws, cudaStream_t st) {
+  CUtensorMap map_w;
+  int rc = map_rows_k(&map_w, desc->wqkv, 3ull * p.d, p.d, 128, "wqkv");
+  if (rc) return rc;
+  auto kern = qkv_lnfused_kernel<KP>;
+  const int smem = QkvLnFusedCfg<KP>::SMEM;
+  if ((rc = ensure_smem((const void*)kern, smem))) return rc;
+  const long long blocks = (p.T + 127) / 128;
+  kern<<<(unsigned)blocks, 256, smem, st>>>(map_w, x, desc->ln1_w, desc->ln1_b, desc->eps1, desc->bqkv, qkv_out(p, ws),
+                                            p.T, p.d, reinterpret_cast<DevStatus*>(ws));
+  return check_launch("qkv_lnfused_kernel");
+}
+
+template <int BN, int ST, int EPI>
+int launch_gemm_tma_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const EpiArgs& ea, long long T, int K, int N,
+                      void* ws, cudaStream_t st) {
+  auto kern = gemm_tma_kernel<BN, ST, EPI>;
+  const int smem = GemmTmaCfg<BN, ST>::SMEM;
+  int rc = ensure_smem((const void*)kern, smem);
+  if (rc) return rc;
+  const long long blocks = ((T + 127) / 128) * ((N + BN - 1) / BN);
+  if (blocks > 0x7fffffffLL) return fail(B200L_ERR_BAD_SHAPE, "grid too large");
+  kern<<<(unsigned)blocks, 192, smem, st>>>(map_a, map_b, ea, T, K, N, reinterpret_cast<DevStatus*>(ws));
+  return check_launch("gemm_tma_kernel");
+}
+
+int run_qkv(const b200l_layer_desc* desc, const Plan& p, const float* x, void* ws, cudaStream_t st) {
+  if (p.d <= 256) {
+    const int kp = (p.d + 63) / 64 * 64;
+    switch (kp) {
+      case 64: return launch_qkv_lnfused_t<64>(desc, p, x, ws, st);
+      case 128: return launch_qkv_lnfused_t<128>(desc, p, x, ws, st);
+      case 192: return launch_qkv_lnfused_t<192>(desc, p, x, ws, st);
+      default: return launch_qkv_lnfused_t<256>(desc, p, x, ws, st);
+    }
+  }
+  // d > 256: row LayerNorm to fp16 h, then the TMA-fed GEMM with the QKV epilogue.
+  __half* h = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + p.off_h);
+  int rc = launch_row_ln<true>(x, h, desc->ln1_w, desc->ln1_b, desc->eps1, p.T, p.d, st);
+  if (rc) return rc;
+  CUtensorMap map_a, map_b;
+  if ((rc = map_rows_k(&map_a, h, (unsigned long long)p.T, p.d, 128, "h"))) return rc;
+  if ((rc = map_rows_k(&map_b, desc->wqkv, 3ull * p.d, p.d, 256, "wqkv"))) return rc;
+  EpiArgs ea{};
+  ea.qkv = qkv_out(p, ws);
+  ea.bias = desc->bqkv;
+  ea.d = p.d;
+  return launch_gemm_tma_t<256, 4, EPI_QKV>(map_a, map_b, ea, p.T, p.d, 3 * p.d, ws, st);
+}
+
+template <int DHP, int BN>
+int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, void* ws, cudaStream_t st) {
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  const unsigned long long BH = (unsigned long long)p.B * p.H;
+  CUtensorMap mq, mk, mv;
+  const CUtensorMapSwizzle qk_swz = DHP >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const unsigned qk_inner = DHP >= 64 ? 64 : 32;
+  {
+    const unsigned long long dims[3] = {(unsigned long long)DHP, (unsigned long long)p.S, BH};
+    const unsigned long long strides[2] = {(unsigned long long)DHP * 2, (unsigned long long)p.S * DHP * 2};
+    const unsigned box_q[3] = {qk_inner, 128, 1};
+    const unsigned box_k[3] = {qk_inner, (unsigned)BN, 1};
+    int rc = make_map(&mq, w + p.off_q, 3, dims, strides, box_q, qk_swz, "q");
+    if (rc) return rc;
+    if ((rc = make_map(&mk, w + p.off_k, 3, dims, strides, box_k, qk_swz, "k"))) return rc;
+  }
+  {
+    const unsigned long long dims[3] = {(unsigned long long)p.S, (unsigned long long)DHP, BH};
+    const unsigned long long strides[2] = {(unsigned long long)p.sp * 2, (unsigned long long)DHP * p.sp * 2};
+    const unsigned box[3] = {64, (unsigned)DHP, 1};
+    int rc = make_map(&mv, w + p.off_vt, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "v^T");
+    if (rc) return rc;
+  }
+  AttnArgs a;
+  a.ctx = reinterpret_cast<__half*>(w + p.off_ctx);
+  a.B = p.B; a.S = p.S; a.H = p.H; a.dh = p.dh; a.d = p.d;
+  a.causal = desc->causal ? 1 : 0;
+  a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)p.dh));
+  a.num_items = (int)(BH * (unsigned long long)((p.S + 127) / 128));
+  auto kern = attn_kernel<DHP, BN>;
+  const int smem = AttnCfg<DHP, BN>::SMEM;
+  int rc = ensure_smem((const void*)kern, smem);
+  if (rc) return rc;
+  const int grid = a.num_items < dev.sms ? a.num_items : dev.sms;
+  kern<<<grid, 192, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
+  return check_launch("attn_kernel");
+}
+
+int run_attn(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, void* ws, cudaStream_t st) {
+  switch (p.dhp) {
+    case 32: return launch_attn_t<32, 128>(desc, p, dev, ws, st);
+    case 64: return launch_attn_t<64, 128>(desc, p, dev, ws, st);
+    case 128: return launch_attn_t<128, 128>(desc, p, dev, ws, st);
+    default: return launch_attn_t<256, 64>(desc, p, dev, ws, st);
+  }
+}
+
+int run_outproj(const b200l_layer_desc* desc, const Plan& p, const float* x, float* y, void* ws, cudaStream_t st) {
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  const __half* ctx = reinterpret_cast<const __half*>(w + p.off_ctx);
+  EpiArgs ea{};
+  ea.bias = desc->bo;
+  ea.x = x;
+  ea.y = y;
+  ea.ln_w = desc->ln2_w;
+  ea.ln_b = desc->ln2_b;
+  ea.eps = desc->eps2;
+  ea.d = p.d;
+  CUtensorMap map_a, map_b;
+  int rc = map_rows_k(&map_a, ctx, (unsigned long long)p.T, p.d, 128, "ctx");
+  if (rc) return rc;
+  if (p.d <= 256) {
+    const int bn = (p.d + 63) / 64 * 64;
+    if ((rc = map_rows_k(&map_b, desc->wo, (unsigned long long)p.d, p.d, (unsigned)bn, "wo"))) return rc;
+    switch (bn) {
+      case 64: return launch_gemm_tma_t<64, 2, EPI_RESID_LN>(map_a, map_b, ea, p.T, p.d, p.d, ws, st);
+      case 128: return launch_gemm_tma_t<128, 2, EPI_RESID_LN>(map_a, map_b, ea, p.T, p.d, p.d, ws, st);
+      case 192: return launch_gemm_tma_t<192, 3, EPI_RESID_LN>(map_a, map_b, ea, p.T, p.d, p.d, ws, st);
+      default: return launch_gemm_tma_t<256, 4, EPI_RESID_LN>(map_a, map_b, ea, p.T, p.d, p.d, ws, st);
+    }
+  }
+  if ((rc = map_rows_k(&map_b, desc->wo, (unsigned long long)p.d, p.d, 256, "wo"))) return rc;
+  if ((rc = launch_gemm_tma_t<256, 4, EPI_RESID>(map_a, map_b, ea, p.T, p.d, p.d, ws, st))) return rc;
+  return launch_row_ln<false>(y, y, desc->ln2_w, desc->ln2_b, desc->eps2, p.T, p.d, st);
+}
+
+int check_xy(const void* x, const void* y, bool need_y) {
+  if (!x) return fail(B200L_ERR_NULL_POINTER, "x is NULL");
+  if (reinterpret_cast<uintptr_t>(x) % 16) return fail(B200L_ERR_ALIGNMENT, "x must be 16-byte aligned");
+  if (need_y) {
+    if (!y) return fail(B200L_ERR_NULL_POINTER, "y is NULL");
+    if (reinterpret_cast<uintptr_t>(y) % 16) return fail(B200L_ERR_ALIGNMENT, "y must be 16-byte aligned");
+    if (x == y) return fail(B200L_ERR_BAD_SHAPE, "x and y must not alias");
+  }
+  return B200L_OK;
+}
+
+}  // namespace
+
+// ===================================================================== C ABI
+extern "C" {
+
+int b200l_version(void) { return B200L_ABI_VERSION; }
+
+int b200l_last_error(char* buf, size_t n) {
+  if (buf && n) {
+    const size_t k = g_last_error.size() < n - 1 ? g_last_error.size() : n - 1;
+    memcpy(buf, g_last_error.data(), k);
+    buf[k] = 0;
+  }
+  return (int)g_last_error.size();
+}
+
+size_t b200l_layer_workspace_bytes(const b200l_layer_desc* desc) {
+  Plan p;
+  if (make_plan(desc, &p)) return 0;
+  return p.total;
+}
+
+int b200l_clear_status(void* workspace, void* stream) {
+  if (!workspace) return fail(B200L_ERR_NULL_POINTER, "workspace is NULL");
+  cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(DevStatus), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
+  return B200L_OK;
+}
+
+int b200l_read_status(const void* workspace, void* stream) {
+  if (!workspace) return fail(B200L_ERR_NULL_POINTER, "workspace is NULL");
+  DevStatus s;
+  cudaError_t e = cudaMemcpyAsync(&s, workspace, sizeof(s), cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the status block");
+  if (s.code) fail(s.code, "device status %d recorded by kernel %d (block %d, site %d)", s.code, s.kernel, s.block, s.where);
+  return s.code;
+}
+
+int b200l_pack_weights(int32_t d, const float* wq, const float* wk, const float* wv, const float* bq, const float* bk,
+                       const float* bv, const float* wo, void* wqkv16, float* bqkv32, void* wo16, void* stream) {
+  if (d <= 0) return fail(B200L_ERR_BAD_SHAPE, "d_model must be positive");
+  if (!wq || !wk || !wv || !bq || !bk || !bv || !wo || !wqkv16 || !bqkv32 || !wo16)
+    return fail(B200L_ERR_NULL_POINTER, "b200l_pack_weights: NULL pointer");
+  DevInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  const long long total = 4LL * d * d;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  pack_weights_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      d, wq, wk, wv, bq, bk, bv, wo, static_cast<__half*>(wqkv16), bqkv32, static_cast<__half*>(wo16));
+  return check_launch("pack_weights_kernel");
+}
+
+int b200l_qkv_ln_gemm(const b200l_layer_desc* desc, const float* x, void* workspace, size_t ws_bytes, void* stream) {
+  Plan p;
+  DevInfo dev;
+  int rc = check_common(desc, workspace, ws_bytes, &p, &dev);
+  if (rc) return rc;
+  if ((rc = check_xy(x, nullptr, false))) return rc;
+  return run_qkv(desc, p, x, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int b200l_flash_attn(const b200l_layer_desc* desc, void* workspace, size_t ws_bytes, void* stream) {
+  Plan p;
+  DevInfo dev;
+  int rc = check_common(desc, workspace, ws_bytes, &p, &dev);
+  if (rc) return rc;
+  return run_attn(desc, p, dev, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int b200l_outproj_res_ln(const b200l_layer_desc* desc, const float* x, float* y, void* workspace, size_t ws_bytes,
+                         void* stream) {
+  Plan p;
+  DevInfo dev;
+  int rc = check_common(desc, workspace, ws_bytes, &p, &dev);
+  if (rc) return rc;
+  if ((rc = check_xy(x, y, true))) return rc;
+  return run_outproj(desc, p, x, y, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int b200l_layer_forward(const b200l_layer_desc* desc, const float* x, float* y, void* workspace, size_t ws_bytes,
+                        void* stream) {
+  Plan p;
+  DevInfo dev;
+  int rc = check_common(desc, workspace, ws_bytes, &p, &dev);
+  if (rc) return rc;
+  if ((rc = check_xy(x, y, true))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = run_qkv(desc, p, x, workspace, st))) return rc;
+  if ((rc = run_attn(desc, p, dev, workspace, st))) return rc;
+  return run_outproj(desc, p, x, y, workspace, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,487 @@
+// gemm.cuh -- tcgen05 GEMMs of the layer: K1 (LayerNorm-fused QKV projection)
+// and the TMA-fed GEMM used for the out-projection (K3, with the residual +
+// LayerNorm epilogue) and for the QKV projection when d_model > 256.
+//
+// Both compute D[128 x N] = A[128 x K] * B[N x K]^T with fp16 operands in
+// shared memory (K-major, 128-byte swizzle) and fp32 accumulators in TMEM,
+// issued by one thread (tcgen05.mma.cta_group::1.kind::f16, M = 128).
+// Thread-per-row epilogues: warp w reads TMEM lanes 32*(w%4)..+31, so each
+// thread owns one output row and row reductions need no shuffles.
+//
+// Reference counterparts: _gemm_kernel (torch_transformer_benchmark.py:283-353),
+// _gemm_ln_kernel (:394-463), _add_ln_kernel (:491-535, as used at :1220-1223).
+#pragma once
+
+#include "common.cuh"
+
+namespace b200l {
+
+// Destination of the QKV projection: q, k as [B*H, S, dhp] and v transposed as
+// [B*H, dhp, sp] (sp = S rounded up to 8, so every row stride is 16-byte
+// aligned for TMA), all fp16. Columns dh..dhp-1 are written as zeros.
+struct QkvOut {
+  __half* q;
+  __half* k;
+  __half* vt;
+  int S, H, dh, dhp, sp, d;
+};
+
+// Stores 32 consecutive projection columns [col0, col0+32) of token t.
+// dh is a multiple of 32, so the chunk lies inside one (q|k|v, head) block.
+__device__ __forceinline__ void qkv_store_chunk(const QkvOut& o, const float* __restrict__ bqkv, long long t,
+                                                int col0, const uint32_t (&acc)[32]) {
+  const int which = col0 / o.d;
+  const int within = col0 - which * o.d;
+  const int head = within / o.dh;
+  const int j0 = within - head * o.dh;
+  const long long b = t / o.S;
+  const int s = (int)(t - b * o.S);
+  const long long bh = b * o.H + head;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]) + __ldg(bqkv + col0 + i);
+  const bool pad_tail = (j0 + 32 == o.dh) && (o.dhp > o.dh);
+  if (which < 2) {
+    __half* dst = (which == 0 ? o.q : o.k) + (bh * o.S + s) * (long long)o.dhp + j0;
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      d4[c] = make_uint4(pack_half2(v[8 * c + 0], v[8 * c + 1]), pack_half2(v[8 * c + 2], v[8 * c + 3]),
+                         pack_half2(v[8 * c + 4], v[8 * c + 5]), pack_half2(v[8 * c + 6], v[8 * c + 7]));
+    }
+    if (pad_tail) {
+      uint4* z = reinterpret_cast<uint4*>(dst + 32);
+      for (int c = 0; c < (o.dhp - o.dh) / 8; ++c) z[c] = make_uint4(0, 0, 0, 0);
+    }
+  } else {
+    __half* dst = o.vt + (bh * o.dhp + j0) * (long long)o.sp + s;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) dst[(long long)i * o.sp] = __float2half_rn(v[i]);
+    if (pad_tail) {
+      for (int jj = 32; jj < 32 + (o.dhp - o.dh); ++jj) dst[(long long)jj * o.sp] = __float2half_rn(0.f);
+    }
+  }
+}
+
+// ===========================================================================
+// K1: h = LN1(x) -> [q|k|v] = h Wqkv^T + bqkv, for d_model <= 256.
+//
+// One CTA per 128-token block. All 8 warps normalise the block's rows (warp
+// per row, coalesced fp32 loads, two-pass variance) straight into the fp16
+// A operand in shared memory, where it stays for every N tile, so x is read
+// exactly once and h never touches HBM. Weight tiles [128 x KP] stream in by
+// TMA (2 stages); accumulators are double-buffered in TMEM (2 x 128 columns)
+// so the epilogue of tile n overlaps the MMAs of tile n+1.
+// KP = d rounded up to 64 (the padding columns of A are written as zeros and
+// the weight map's out-of-range columns are zero-filled by TMA).
+// ===========================================================================
+template <int KP>
+struct QkvLnFusedCfg {
+  static constexpr int KC = KP / 64;                // 128-byte atom columns
+  static constexpr int A_BYTES = KC * 128 * 128;    // 128 rows
+  static constexpr int W_BYTES = KC * 128 * 128;    // one 128-row N tile
+  static constexpr int WST = 2;
+  static constexpr int SMEM = A_BYTES + WST * W_BYTES + 256 + 1024;  // + barriers + alignment slack
+  static constexpr int NV = (KP + 127) / 128;       // float4 per lane in the LN prologue
+};
+
+template <int KP>
+__global__ void __launch_bounds__(256, 1)
+    qkv_lnfused_kernel(const __grid_constant__ CUtensorMap map_w, const float* __restrict__ x,
+                       const float* __restrict__ ln_w, const float* __restrict__ ln_b, float eps,
+                       const float* __restrict__ bqkv, QkvOut out, long long T, int d, DevStatus* status) {
+  using C = QkvLnFusedCfg<KP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sW = smem + C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + C::WST * C::W_BYTES);
+  uint64_t* w_full = bars;         // [2]
+  uint64_t* w_empty = bars + 2;    // [2]
+  uint64_t* acc_full = bars + 4;   // [2]
+  uint64_t* acc_empty = bars + 6;  // [2]
+  uint64_t* mma_done = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 10);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long m0 = (long long)blockIdx.x * 128;
+  const int N = 3 * d;
+  const int NT = (N + 127) / 128;
+  const int KS = (d + 15) / 16;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&w_full[i], 1);
+      mbar_init(&w_empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // Start the first weight tiles before the LayerNorm prologue.
+  const int npro = NT < C::WST ? NT : C::WST;
+  if (threadIdx.x == 0) {
+    for (int n = 0; n < npro; ++n) {
+      mbar_arrive_expect_tx(&w_full[n], C::W_BYTES);
+      for (int kc = 0; kc < C::KC; ++kc) tma_load_2d(sW + n * C::W_BYTES + kc * 16384, &map_w, &w_full[n], kc * 64, n * 128);
+    }
+  }
+
+  // ---- LayerNorm prologue: 16 rows per warp, into the swizzled fp16 A tile.
+  {
+    const float inv_d = 1.0f / (float)d;
+    const uint32_t a_base = smem_u32(sA);
+#pragma unroll 1
+    for (int rr = 0; rr < 16; ++rr) {
+      const int row = warp * 16 + rr;
+      const long long t = m0 + row;
+      const bool valid = t < T;
+      float4 v[C::NV];
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < C::NV; ++i) {
+        const int k = (lane + 32 * i) * 4;
+        if (valid && k < d) {
+          v[i] = __ldg(reinterpret_cast<const float4*>(x + t * d + k));
+          s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        } else {
+          v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      const float mean = warp_sum(s) * inv_d;
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < C::NV; ++i) {
+        const int k = (lane + 32 * i) * 4;
+        if (valid && k < d) {
+          const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
+          q += (a * a + b * b) + (c * c + e * e);
+        }
+      }
+      const float rstd = rsqrtf(warp_sum(q) * inv_d + eps);
+#pragma unroll
+      for (int i = 0; i < C::NV; ++i) {
+        const int k = (lane + 32 * i) * 4;
+        if (k < KP) {
+          uint32_t lo = 0, hi = 0;
+          if (valid && k < d) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4*>(ln_w + k));
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(ln_b + k));
+            lo = pack_half2((v[i].x - mean) * rstd * w4.x + b4.x, (v[i].y - mean) * rstd * w4.y + b4.y);
+            hi = pack_half2((v[i].z - mean) * rstd * w4.z + b4.z, (v[i].w - mean) * rstd * w4.w + b4.w);
+          }
+          const int kc = k >> 6, kin = k & 63;
+          st_shared_v2(a_base + kc * 16384 + swz_offset(row, kin >> 3, 128) + (kin & 7) * 2, lo, hi);
+        }
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer for the remaining weight tiles
+      int last[2] = {-1, -1};
+      for (int n = 0; n < npro; ++n) last[n] = n;
+      for (int n = C::WST; n < NT; ++n) {
+        const int s = n % C::WST;
+        if (!mbar_wait(&w_empty[s], ((n / C::WST) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&w_full[s], C::W_BYTES);
+        for (int kc = 0; kc < C::KC; ++kc)
+          tma_load_2d(sW + s * C::W_BYTES + kc * 16384, &map_w, &w_full[s], kc * 64, n * 128);
+        last[s] = n;
+      }
+      for (int s = 0; s < 2; ++s)
+        if (last[s] >= 0) mbar_drain(&w_full[s], (last[s] / C::WST) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      const uint32_t idesc = idesc_f16_f32(128, 128);
+      const uint32_t a_base = smem_u32(sA);
+      for (int n = 0; n < NT; ++n) {
+        const int s = n % C::WST, a = n & 1;
+        if (!mbar_wait(&w_full[s], (n / C::WST) & 1, abort_flag)) break;
+        if (!mbar_wait(&acc_empty[a], ((n >> 1) & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t w_base = smem_u32(sW + s * C::W_BYTES);
+        for (int k = 0; k < KS; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          umma_f16_ss(tmem_base + a * 128, sdesc_kmajor(a_base + off, 128), sdesc_kmajor(w_base + off, 128), idesc,
+                      k > 0 ? 1u : 0u);
+        }
+        umma_commit(&w_empty[s]);
+        umma_commit(&acc_full[a]);
+      }
+      umma_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+  } else if (warp >= 4) {  // ---- epilogue: bias, fp16, scatter to q / k / v^T
+    const int qd = warp & 3;
+    const int row = qd * 32 + lane;
+    const long long t = m0 + row;
+    const bool valid = t < T;
+    for (int n = 0; n < NT; ++n) {
+      const int a = n & 1;
+      if (!mbar_wait(&acc_full[a], (n >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        const int col0 = n * 128 + cc * 32;
+        if (col0 >= N) break;
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(qd * 32) << 16) + a * 128 + cc * 32, r);
+        if (valid) qkv_store_chunk(out, bqkv, t, col0, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kQkvLnFused, 0);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 256);
+  }
+}
+
+// ===========================================================================
+// TMA-fed GEMM: D[128 x BN] = A[128 x K] * B[BN x K]^T over a ST-stage ring of
+// (A 128x64, B BNx64) fp16 tiles, one accumulator of BN TMEM columns.
+// Epilogues:
+//   EPI_QKV       bias + scatter into q / k / v^T        (QKV for d > 256)
+//   EPI_RESID     y = x + acc + bias  (fp32, pre-LN)      (out-proj for d > 256)
+//   EPI_RESID_LN  y = LN2(x + acc + bias), BN >= d        (out-proj for d <= 256)
+// The residual is added to the fp32 accumulator and never rounded to fp16
+// before the add (the reference's fp32-store rule, :187-191, :350-353).
+// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-5 epilogue.
+// ===========================================================================
+enum EpiKind : int { EPI_QKV = 0, EPI_RESID = 1, EPI_RESID_LN = 2 };
+
+struct EpiArgs {
+  QkvOut qkv;
+  const float* bias;
+  const float* x;
+  float* y;
+  const float* ln_w;
+  const float* ln_b;
+  float eps;
+  int d;
+};
+
+template <int BN, int ST>
+struct GemmTmaCfg {
+  static constexpr int A_BYTES = 128 * 128;  // 128 rows x 64 fp16
+  static constexpr int B_BYTES = BN * 128;   // BN rows x 64 fp16
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int SMEM = ST * STAGE + 256 + 1024;
+  static constexpr int TMEM_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+};
+
+template <int BN, int ST, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                    EpiArgs ea, long long T, int K, int N, DevStatus* status) {
+  using C = GemmTmaCfg<BN, ST>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST * C::STAGE);
+  uint64_t* full = bars;             // [ST]
+  uint64_t* empty = bars + ST;       // [ST]
+  uint64_t* acc_full = bars + 2 * ST;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * ST + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NT = (N + BN - 1) / BN;
+  const long long m0 = (long long)(blockIdx.x / NT) * 128;
+  const int n0 = (blockIdx.x % NT) * BN;
+  const int KT = (K + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- producer
+      int last[ST];
+      for (int i = 0; i < ST; ++i) last[i] = -1;
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % ST;
+        if (!mbar_wait(&empty[s], ((kt / ST) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        uint8_t* st = smem + s * C::STAGE;
+        tma_load_2d(st, &map_a, &full[s], kt * 64, (int)m0);
+        tma_load_2d(st + C::A_BYTES, &map_b, &full[s], kt * 64, n0);
+        last[s] = kt;
+      }
+      for (int s = 0; s < ST; ++s)
+        if (last[s] >= 0) mbar_drain(&full[s], (last[s] / ST) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      const uint32_t idesc = idesc_f16_f32(128, BN);
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % ST;
+        if (!mbar_wait(&full[s], (kt / ST) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + s * C::STAGE);
+        const uint32_t b_base = a_base + C::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16_ss(tmem_base, sdesc_kmajor(a_base + kk * 32, 128), sdesc_kmajor(b_base + kk * 32, 128), idesc,
+                      (kt | kk) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(acc_full);
+      mbar_drain(acc_full, 0);
+    }
+  } else {  // ---- epilogue warps 2..5
+    const int qd = warp & 3;
+    const int row = qd * 32 + lane;
+    const long long t = m0 + row;
+    const bool valid = t < T;
+    const uint32_t tl = tmem_base + ((uint32_t)(qd * 32) << 16);
+    if (mbar_wait(acc_full, 0, abort_flag)) {
+      tc_fence_after();
+      if constexpr (EPI == EPI_QKV) {
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          const int col0 = n0 + cc * 32;
+          if (col0 >= N) break;
+          uint32_t r[32];
+          tmem_ld32(tl + cc * 32, r);
+          if (valid) qkv_store_chunk(ea.qkv, ea.bias, t, col0, r);
+        }
+      } else if constexpr (EPI == EPI_RESID) {
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          const int col0 = n0 + cc * 32;
+          if (col0 >= N) break;
+          uint32_t r[32];
+          tmem_ld32(tl + cc * 32, r);
+          if (valid) {
+            const float* xr = ea.x + t * ea.d + col0;
+            float* yr = ea.y + t * ea.d + col0;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const float4 xv = __ldg(reinterpret_cast<const float4*>(xr) + c);
+              const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.bias + col0) + c);
+              float4 o;
+              o.x = xv.x + (__uint_as_float(r[4 * c + 0]) + bv.x);
+              o.y = xv.y + (__uint_as_float(r[4 * c + 1]) + bv.y);
+              o.z = xv.z + (__uint_as_float(r[4 * c + 2]) + bv.z);
+              o.w = xv.w + (__uint_as_float(r[4 * c + 3]) + bv.w);
+              reinterpret_cast<float4*>(yr)[c] = o;
+            }
+          }
+        }
+      } else {  // EPI_RESID_LN: the whole row is in this tile (n0 == 0, BN >= d)
+        const int d = ea.d;
+        const float* xr = ea.x + t * d;
+        float sum = 0.f;
+        // pass 1: r = x + (acc + b), written back into TMEM; row sum.
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tl + cc * 32, r);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int col = cc * 32 + 4 * c;
+            if (valid && col < d) {
+              const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + col));
+              const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.bias + col));
+              const float a0 = xv.x + (__uint_as_float(r[4 * c + 0]) + bv.x);
+              const float a1 = xv.y + (__uint_as_float(r[4 * c + 1]) + bv.y);
+              const float a2 = xv.z + (__uint_as_float(r[4 * c + 2]) + bv.z);
+              const float a3 = xv.w + (__uint_as_float(r[4 * c + 3]) + bv.w);
+              sum += (a0 + a1) + (a2 + a3);
+              r[4 * c + 0] = __float_as_uint(a0);
+              r[4 * c + 1] = __float_as_uint(a1);
+              r[4 * c + 2] = __float_as_uint(a2);
+              r[4 * c + 3] = __float_as_uint(a3);
+            }
+          }
+          tmem_st32(tl + cc * 32, r);
+        }
+        const float inv_d = 1.0f / (float)d;
+        const float mean = sum * inv_d;
+        // pass 2: variance about the mean.
+        float sq = 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tl + cc * 32, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = cc * 32 + i;
+            if (col < d) {
+              const float dv = __uint_as_float(r[i]) - mean;
+              sq += dv * dv;
+            }
+          }
+        }
+        const float rstd = rsqrtf(sq * inv_d + ea.eps);
+        // pass 3: normalise and store.
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tl + cc * 32, r);
+          if (valid) {
+            float* yr = ea.y + t * d;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int col = cc * 32 + 4 * c;
+              if (col < d) {
+                const float4 wv = __ldg(reinterpret_cast<const float4*>(ea.ln_w + col));
+                const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.ln_b + col));
+                float4 o;
+                o.x = (__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bv.x;
+                o.y = (__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bv.y;
+                o.z = (__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bv.z;
+                o.w = (__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bv.w;
+                *reinterpret_cast<float4*>(yr + col) = o;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kGemmTma, EPI);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace b200l

@@ -1,0 +1,144 @@
+/*
+ * cobra_b200.h -- C ABI of the B200 (sm_100a) single transformer-layer forward.
+ *
+ * The reference (dalberrt/COBRA-GPU-Kernel, torch_transformer_benchmark.py) is
+ * pure Python: its drop-in is the nn.Module ``UserOptimizedTransformer``
+ * (:917-1541) whose forward drives Triton kernels. This header is the native
+ * boundary underneath the equivalent module of this repository; every entry
+ * point names the reference function it replaces.
+ *
+ * Conventions
+ *   - Plain pointers are device pointers on the current CUDA device unless
+ *     stated otherwise. ``stream`` is a cudaStream_t passed as void*.
+ *   - Every call is asynchronous on ``stream``, allocates nothing, never
+ *     synchronises the host, and is safe to capture in a CUDA graph.
+ *   - Return value: B200L_OK (0) or a negative B200L_ERR_* code; the message
+ *     of the last failure on the calling thread is available through
+ *     b200l_last_error().
+ *   - Device-side failures (a pipeline wait that exceeded its time limit) are
+ *     recorded in the status word at the start of the workspace and read with
+ *     b200l_read_status(); kernels never trap.
+ *
+ * Layout (T = batch*seq_len tokens, d = d_model, H heads, dh = d/H,
+ * dhp = dh rounded up to 32/64/128/256):
+ *   x, y      fp32 [T, d] row-major (the reference's [B,S,d] tensors)
+ *   wqkv      fp16 [3d, d]  rows q(0..d-1), k(d..2d-1), v(2d..3d-1); nn.Linear
+ *             weight layout, i.e. K-major (torch_transformer_benchmark.py:876-883)
+ *   bqkv      fp32 [3d]
+ *   wo        fp16 [d, d];  bo fp32 [d]
+ *   ln*_w/_b  fp32 [d]
+ *   workspace (bytes from b200l_layer_workspace_bytes), 1024-byte aligned,
+ *             every region 1024-aligned (sp = S rounded up to 8):
+ *             [status 256 B][q fp16 B*H*S*dhp][k fp16 B*H*S*dhp]
+ *             [v^T fp16 B*H*dhp*sp][ctx fp16 T*d][h fp16 T*d, only d > 256]
+ */
+#ifndef COBRA_B200_H
+#define COBRA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200L_API __attribute__((visibility("default")))
+#else
+#define B200L_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200L_ABI_VERSION 1
+
+enum b200l_status {
+    B200L_OK = 0,
+    B200L_ERR_BAD_SHAPE = -1,          /* non-positive size, d % H != 0, d > 2048, aliasing */
+    B200L_ERR_UNSUPPORTED_HEAD_DIM = -2, /* d/H not a multiple of 32 in [32, 256] */
+    B200L_ERR_NULL_POINTER = -3,
+    B200L_ERR_WORKSPACE_TOO_SMALL = -4,
+    B200L_ERR_LAUNCH = -5,             /* a CUDA launch or attribute call failed */
+    B200L_ERR_DEVICE = -6,             /* not an sm_100 device */
+    B200L_ERR_TIMEOUT = -7,            /* a device pipeline wait ran out (status word) */
+    B200L_ERR_ALIGNMENT = -8           /* a pointer is not 16-byte aligned */
+};
+
+/* Layer description. Replaces the per-layer state the reference keeps in
+ * ``_LayerPack`` (torch_transformer_benchmark.py:857-914) plus the shape and
+ * policy fields ``_prepare`` derives (:948-1081). */
+typedef struct b200l_layer_desc {
+    int32_t batch;        /* B */
+    int32_t seq_len;      /* S */
+    int32_t d_model;      /* d <= 2048 */
+    int32_t num_heads;    /* H, d % H == 0, d/H a multiple of 32 in [32, 256] */
+    int32_t causal;       /* 0: full attention (the judged mode), 1: causal */
+    float eps1;           /* norm1 eps (nn.LayerNorm default 1e-5) */
+    float eps2;           /* norm2 eps */
+    const void* wqkv;     /* fp16 [3d, d] */
+    const float* bqkv;    /* fp32 [3d] */
+    const void* wo;       /* fp16 [d, d] */
+    const float* bo;      /* fp32 [d] */
+    const float* ln1_w;   /* fp32 [d] */
+    const float* ln1_b;
+    const float* ln2_w;
+    const float* ln2_b;
+} b200l_layer_desc;
+
+/* ABI version (B200L_ABI_VERSION). */
+B200L_API int b200l_version(void);
+
+/* Copies the last error message of the calling thread into buf (NUL-terminated,
+ * truncated to n bytes); returns the length of the full message. */
+B200L_API int b200l_last_error(char* buf, size_t n);
+
+/* Bytes of workspace b200l_layer_forward needs for this description.
+ * Replaces the reference's live-set estimate ``_activation_bytes_per_seq``
+ * (torch_transformer_benchmark.py:1364-1400), but exact. */
+B200L_API size_t b200l_layer_workspace_bytes(const b200l_layer_desc* desc);
+
+/* Zeroes the status word at the start of a workspace (async on stream). */
+B200L_API int b200l_clear_status(void* workspace, void* stream);
+
+/* Reads the status word (synchronises ``stream``): 0 when no kernel recorded a
+ * failure, else the B200L_ERR_* code that was recorded. */
+B200L_API int b200l_read_status(const void* workspace, void* stream);
+
+/* Packs nn.Linear weights into the layout above: wqkv = cast_fp16(cat(wq, wk,
+ * wv)), bqkv = cat(bq, bk, bv), wo16 = cast_fp16(wo). Inputs fp32 on device.
+ * Replaces ``_LayerPack.__init__`` (torch_transformer_benchmark.py:873-914). */
+B200L_API int b200l_pack_weights(int32_t d_model, const float* wq, const float* wk, const float* wv,
+                       const float* bq, const float* bk, const float* bv, const float* wo,
+                       void* wqkv16, float* bqkv32, void* wo16, void* stream);
+
+/* The whole layer: y = LN2(x + Attn(LN1(x)) Wo^T + bo). x and y must not alias.
+ * Replaces ``UserOptimizedTransformer._run_fused`` for one layer
+ * (torch_transformer_benchmark.py:1170-1327: lines 1216-1223, 1227-1238,
+ * 1262-1268) and, as the module's forward, ``forward`` (:1512-1541). */
+B200L_API int b200l_layer_forward(const b200l_layer_desc* desc, const float* x, float* y,
+                        void* workspace, size_t ws_bytes, void* stream);
+
+/* K1: h = LN1(x) fused into the QKV projection on tcgen05; writes q, k
+ * ([B,H,S,dhp] fp16) and v^T ([B,H,dhp,S] fp16) into the workspace.
+ * Replaces ``_tl_add_ln`` (:539-569, used at :1220-1223) + ``F.linear``/
+ * ``_gemm_kernel`` for qkv (:283-381, :1234). */
+B200L_API int b200l_qkv_ln_gemm(const b200l_layer_desc* desc, const float* x,
+                      void* workspace, size_t ws_bytes, void* stream);
+
+/* K2: ctx = softmax(q k^T / sqrt(dh)) v per (batch, head), flash-style on
+ * tcgen05, scores never written to memory; reads q/k/v^T from the workspace
+ * and writes ctx fp16 [T, d] into it. Replaces ``_tl_attn``/``_attn_kernel``
+ * (:572-649, :828-854) and the SDPA fallback (:1239-1253). */
+B200L_API int b200l_flash_attn(const b200l_layer_desc* desc, void* workspace, size_t ws_bytes,
+                     void* stream);
+
+/* K3: y = LN2(x + ctx Wo^T + bo) on tcgen05 with the residual and LayerNorm in
+ * the epilogue (for d > 256 the epilogue stores the residual and a row
+ * LayerNorm pass follows). Replaces ``_tl_linear_ln``/``_gemm_ln_kernel``
+ * (:394-488, used at :1262-1268). */
+B200L_API int b200l_outproj_res_ln(const b200l_layer_desc* desc, const float* x, float* y,
+                         void* workspace, size_t ws_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COBRA_B200_H */

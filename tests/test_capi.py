@@ -1,0 +1,75 @@
+"""CPU tests of the C ABI: the library builds, loads, exports every declared
+symbol, and validates shapes before touching a device."""
+
+import ctypes
+import re
+
+import pytest
+
+from tests.conftest import ROOT
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        names |= set(re.findall(r"B200L_API\s+[\w\s\*]+?\b(b200l_\w+)\s*\(", h.read_text()))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for n in ("b200l_layer_forward", "b200l_qkv_ln_gemm", "b200l_flash_attn",
+              "b200l_outproj_res_ln", "b200l_pack_weights", "b200l_last_error", "b200l_version"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._lib.lib()
+    handle = ctypes.CDLL(lib._name)
+    for n in declared_symbols():
+        assert hasattr(handle, n), f"{n} declared in include/ but not exported"
+    assert set(pkg._lib.EXPORTED) == declared_symbols()
+    assert lib.b200l_version() == pkg._lib.ABI_VERSION
+
+
+def _desc(pkg, B, S, d, H):
+    return pkg._lib.LayerDesc(batch=B, seq_len=S, d_model=d, num_heads=H, causal=0, eps1=1e-5, eps2=1e-5)
+
+
+@pytest.mark.parametrize("B,S,d,H", [(4, 128, 128, 4), (3, 17, 96, 3), (10000, 128, 128, 4),
+                                     (32, 100000, 1024, 16), (2, 96, 256, 1), (2, 200, 512, 4)])
+def test_workspace_bytes_matches_python_layout(pkg, B, S, d, H):
+    lib = pkg._lib.lib()
+    d_ = _desc(pkg, B, S, d, H)
+    n = lib.b200l_layer_workspace_bytes(ctypes.byref(d_))
+    assert n == pkg._lib.workspace_layout(B, S, d, H)["total"]
+    assert n % 1024 == 0
+
+
+@pytest.mark.parametrize("B,S,d,H,code,msg", [
+    (0, 128, 128, 4, -1, "positive"),
+    (2, 128, 130, 4, -1, "divisible"),
+    (2, 128, 48, 3, -2, "head_dim 16"),
+    (2, 128, 640, 1, -2, "head_dim 640"),
+    (2, 128, 4096, 16, -1, "2048"),
+])
+def test_bad_shapes_are_rejected_on_the_host(pkg, B, S, d, H, code, msg):
+    lib = pkg._lib.lib()
+    d_ = _desc(pkg, B, S, d, H)
+    assert lib.b200l_layer_workspace_bytes(ctypes.byref(d_)) == 0
+    rc = lib.b200l_layer_forward(ctypes.byref(d_), None, None, None, 0, None)
+    assert rc == code
+    assert msg in pkg._lib.last_error()
+
+
+def test_null_descriptor(pkg):
+    lib = pkg._lib.lib()
+    assert lib.b200l_layer_forward(None, None, None, None, 0, None) == -3
+    assert lib.b200l_flash_attn(None, None, 0, None) == -3
+
+
+def test_no_cpu_fallback(pkg):
+    import torch
+    layer = pkg.B200TransformerLayer(128, 4)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        layer(torch.zeros(1, 4, 128))

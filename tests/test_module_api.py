@@ -1,0 +1,41 @@
+"""CPU tests of the drop-in module's API (no kernels run)."""
+
+import pytest
+import torch
+
+from oracle import ReferenceLayer, TransformerConfig, build_reference_layer
+
+
+def test_state_dict_identical_keys_and_strict_load(pkg):
+    ref = build_reference_layer(TransformerConfig(2, 8, 128, 4), 1234)
+    lay = pkg.B200TransformerLayer(128, 4)
+    assert set(lay.state_dict()) == set(ref.state_dict())
+    lay.load_state_dict(ref.state_dict(), strict=True)      # must not raise
+    for k, v in ref.state_dict().items():
+        assert torch.equal(lay.state_dict()[k], v)
+
+
+def test_same_seed_same_init_as_reference(pkg):
+    torch.manual_seed(42)
+    a = ReferenceLayer(96, 3)
+    torch.manual_seed(42)
+    b = pkg.B200TransformerLayer(96, 3)
+    for k, v in a.state_dict().items():
+        assert torch.equal(b.state_dict()[k], v)
+
+
+def test_from_config_mirrors_reference_config(pkg):
+    cfg = pkg.TransformerConfig(4, 128, 128, 4, causal=True)
+    lay = pkg.B200TransformerLayer.from_config(cfg)
+    assert lay.causal and lay.attention.head_dim == 32
+    with pytest.raises(ValueError):
+        pkg.TransformerConfig(4, 128, 130, 4).validate()
+    with pytest.raises(ValueError):
+        pkg.TransformerConfig(4, 128, 128, 4, num_layers=2).validate()
+
+
+def test_load_state_dict_invalidates_pack(pkg):
+    lay = pkg.B200TransformerLayer(64, 2)
+    lay._pack = object()
+    lay.load_state_dict(ReferenceLayer(64, 2).state_dict())
+    assert lay._pack is None
