@@ -17,10 +17,13 @@ EXPORTED = (
     "b200l_version", "b200l_last_error", "b200l_layer_workspace_bytes",
     "b200l_clear_status", "b200l_read_status", "b200l_pack_weights",
     "b200l_layer_forward", "b200l_qkv_ln_gemm", "b200l_flash_attn",
-    "b200l_outproj_res_ln",
+    "b200l_outproj_res_ln", "b200l_layer_forward_noalloc",
 )
 
 ABI_VERSION = 1
+
+# Size of the library's built-in scratch used by b200l_layer_forward_noalloc.
+NOALLOC_MAX_SCRATCH_BYTES = 64 * 1024 * 1024
 
 ERRORS = {
     -1: "B200L_ERR_BAD_SHAPE",
@@ -70,6 +73,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "b200l_qkv_ln_gemm": (c_int, [P, P, P, c_size_t, P]),
         "b200l_flash_attn": (c_int, [P, P, c_size_t, P]),
         "b200l_outproj_res_ln": (c_int, [P, P, P, P, c_size_t, P]),
+        "b200l_layer_forward_noalloc": (c_int, [P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -459,3 +459,59 @@ int b200l_layer_forward(const b200l_layer_desc* desc, const float* x, float* y, 
 }
 
 }  // extern "C"
+
+// ===================================================================== no-alloc variant
+// b200l_layer_forward_noalloc: the same three kernels as b200l_layer_forward,
+// but the scratch they need (status block, q, k, v^T, ctx, h) lives in a
+// fixed array inside this library instead of a caller-provided workspace.
+// It exists for callers that cannot call cudaMalloc themselves -- a plugin
+// inside a host process whose device memory is owned by its own pool, or a
+// latency-critical service that forbids allocation after start-up because
+// cudaMalloc/cudaFree synchronise the device.
+//
+// The array is B200L_NOALLOC_MAX_SCRATCH_BYTES (64 MiB) plus 1 KiB so the
+// regions can start on a 1024-byte boundary; every GPU that loads this
+// library holds it until the process exits. Device code could name it
+// directly, but in host code its name is only a host-side stand-in, so the
+// device address is looked up with cudaGetSymbolAddress on the first call on
+// each device (with that device current) and cached.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[B200L_NOALLOC_MAX_SCRATCH_BYTES + 1024];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_base[64] = {nullptr};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B200L_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_base[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_base[dev] = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+  }
+  *out = g_noalloc_base[dev];
+  return B200L_OK;
+}
+}  // namespace
+
+extern "C" int b200l_layer_forward_noalloc(const b200l_layer_desc* desc, const float* x, float* y, void* stream) {
+  Plan p;
+  int rc = make_plan(desc, &p);
+  if (rc) return rc;
+  if (p.total > (size_t)B200L_NOALLOC_MAX_SCRATCH_BYTES)
+    return fail(B200L_ERR_WORKSPACE_TOO_SMALL,
+                "b200l_layer_forward_noalloc: this problem needs %zu bytes of scratch but the built-in scratch holds "
+                "%zu; call b200l_layer_forward with a workspace instead",
+                p.total, (size_t)B200L_NOALLOC_MAX_SCRATCH_BYTES);
+  void* ws = nullptr;
+  if ((rc = noalloc_scratch(&ws))) return rc;
+  // The status block must start at zero for this call; everything else the
+  // kernels read is written earlier in the same call.
+  cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(DevStatus), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc status)");
+  return b200l_layer_forward(desc, x, y, ws, (size_t)B200L_NOALLOC_MAX_SCRATCH_BYTES, stream);
+}

@@ -137,6 +137,29 @@ B200L_API int b200l_flash_attn(const b200l_layer_desc* desc, void* workspace, si
 B200L_API int b200l_outproj_res_ln(const b200l_layer_desc* desc, const float* x, float* y,
                          void* workspace, size_t ws_bytes, void* stream);
 
+/* Allocation-free variant of b200l_layer_forward. No counterpart in the
+ * reference (its Python module always allocates through PyTorch).
+ *
+ * For callers that cannot call cudaMalloc: a plugin whose host process owns
+ * all device memory through its own pool, or a latency-critical service that
+ * forbids allocation after start-up (cudaMalloc/cudaFree synchronise the
+ * device). The scratch the kernels need comes from a fixed array of
+ * B200L_NOALLOC_MAX_SCRATCH_BYTES inside the library, which every GPU that
+ * loads the library holds until exit; problems whose workspace
+ * (b200l_layer_workspace_bytes) exceeds it are rejected with
+ * B200L_ERR_WORKSPACE_TOO_SMALL. The caller still passes x and y.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - Nothing is allocated or freed; the status block at the start of the
+ *     array is cleared (cudaMemsetAsync) at the start of every call.
+ *   - All calls on a device share the one array and it keeps the last call's
+ *     contents: calls that overlap on the GPU (different streams without
+ *     ordering between them) race and corrupt each other's results. */
+#define B200L_NOALLOC_MAX_SCRATCH_BYTES (64u * 1024u * 1024u)
+B200L_API int b200l_layer_forward_noalloc(const b200l_layer_desc* desc, const float* x, float* y,
+                                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif
