@@ -223,9 +223,13 @@ def main() -> int:
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the config's batch (smaller cases for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = dict(CONFIGS[args.config])
+    if args.batch > 0:
+        cfg["B"] = args.batch
 
     if args.impl == "reference":
         return run_reference_arm(args, cfg)
