@@ -20,6 +20,7 @@
 #include "../../include/cobra_b200.h"
 #include "attn.cuh"
 #include "common.cuh"
+#include "fused_layer.cuh"
 #include "gemm.cuh"
 #include "rowln.cuh"
 
@@ -353,6 +354,38 @@ int run_outproj(const b200l_layer_desc* desc, const Plan& p, const float* x, flo
   return launch_row_ln<false>(y, y, desc->ln2_w, desc->ln2_b, desc->eps2, p.T, p.d, st);
 }
 
+// Whole-layer kernel for d_model in {64, 128}, head_dim 32, S <= 128.
+bool fused_eligible(const Plan& p) { return (p.d == 64 || p.d == 128) && p.dh == 32 && p.S <= 128; }
+
+template <int DM>
+int launch_fused_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, const float* x, float* y, void* ws,
+                   cudaStream_t st) {
+  CUtensorMap map_wqkv, map_wo;
+  int rc = map_rows_k(&map_wqkv, desc->wqkv, 3ull * DM, DM, 32, "wqkv");
+  if (rc) return rc;
+  if ((rc = map_rows_k(&map_wo, desc->wo, (unsigned long long)DM, DM, DM, "wo"))) return rc;
+  FusedArgs a;
+  a.x = x; a.y = y;
+  a.ln1_w = desc->ln1_w; a.ln1_b = desc->ln1_b; a.eps1 = desc->eps1;
+  a.bqkv = desc->bqkv; a.bo = desc->bo;
+  a.ln2_w = desc->ln2_w; a.ln2_b = desc->ln2_b; a.eps2 = desc->eps2;
+  a.B = p.B; a.S = p.S; a.causal = desc->causal ? 1 : 0;
+  a.scale_log2 = (float)(1.4426950408889634 / sqrt(32.0));
+  auto kern = fused_layer_kernel<DM>;
+  const int smem = FusedCfg<DM>::SMEM;
+  if ((rc = ensure_smem((const void*)kern, smem))) return rc;
+  const int npairs = (p.B + 1) / 2;
+  const int grid = npairs < dev.sms ? npairs : dev.sms;
+  kern<<<grid, 384, smem, st>>>(map_wqkv, map_wo, a, reinterpret_cast<DevStatus*>(ws));
+  return check_launch("fused_layer_kernel");
+}
+
+int run_fused(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, const float* x, float* y, void* ws,
+              cudaStream_t st) {
+  if (p.d == 128) return launch_fused_t<128>(desc, p, dev, x, y, ws, st);
+  return launch_fused_t<64>(desc, p, dev, x, y, ws, st);
+}
+
 int check_xy(const void* x, const void* y, bool need_y) {
   if (!x) return fail(B200L_ERR_NULL_POINTER, "x is NULL");
   if (reinterpret_cast<uintptr_t>(x) % 16) return fail(B200L_ERR_ALIGNMENT, "x must be 16-byte aligned");
@@ -453,6 +486,7 @@ int b200l_layer_forward(const b200l_layer_desc* desc, const float* x, float* y, 
   if (rc) return rc;
   if ((rc = check_xy(x, y, true))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (fused_eligible(p)) return run_fused(desc, p, dev, x, y, workspace, st);
   if ((rc = run_qkv(desc, p, x, workspace, st))) return rc;
   if ((rc = run_attn(desc, p, dev, workspace, st))) return rc;
   return run_outproj(desc, p, x, y, workspace, st);

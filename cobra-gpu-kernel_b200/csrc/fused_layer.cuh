@@ -1,0 +1,468 @@
+// fused_layer.cuh -- the whole layer in one persistent kernel for short
+// sequences: y = LN2(x + Attn(LN1(x)) Wo^T + bo) with d_model in {64, 128},
+// head_dim 32 and S <= 128 (BASELINE cfg1 / cfg2 shapes).
+//
+// One sequence (<= 128 tokens) fills the M = 128 rows of every tcgen05 tile,
+// so h, q, k, v, the scores and ctx never leave the SM: per sequence the only
+// HBM traffic is x in (read again for the residual, normally an L2 hit) and y
+// out -- the layer's algorithmic 8*T*d bytes -- against 36*T*d for the
+// three-kernel path. This is the B200 form of the reference's fused
+// QKV+attention kernel (_qkvattn_kernel, torch_transformer_benchmark.py:654-741)
+// carried through the out-projection and both LayerNorms.
+//
+// Two sequences are processed in lockstep, one per worker warpgroup, so the
+// tensor core alternates between them while the other one is in its
+// LayerNorm / softmax / epilogue. Per sequence slot, TMEM (256 columns):
+//   [0, 96)    q|k|v projection of one head (fp32)    -- later the out-proj acc [0, d)
+//   [96, 112)  q of the head as fp16 pairs (A operand of S = q k^T, read from TMEM)
+//   [96, 128)  O = P v of the head (fp32)
+//   [128, 256) S = q k^T (fp32); P (fp16 pairs) overwrites [128, 192) in place
+// Shared memory per slot: A = LN1(x) fp16 (kept for every head's projection),
+// C = ctx fp16 (A operand of the out-projection), k [128 x 32] and v^T [32 x 128]
+// fp16 of the current head. Weight tiles (q|k|v rows of one head, then Wo)
+// stream from L2 through a 2-deep TMA ring shared by both slots.
+// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 4-7 slot-0 rows,
+// 8-11 slot-1 rows (one token row per thread).
+#pragma once
+
+#include "common.cuh"
+
+namespace b200l {
+
+struct FusedArgs {
+  const float* x;
+  float* y;
+  const float* ln1_w;
+  const float* ln1_b;
+  const float* bqkv;
+  const float* bo;
+  const float* ln2_w;
+  const float* ln2_b;
+  float eps1, eps2;
+  int B, S;
+  int causal;
+  float scale_log2;
+};
+
+template <int DM>
+struct FusedCfg {
+  static constexpr int H = DM / 32;
+  static constexpr int KC = DM / 64;                 // 128-byte atom columns along d
+  static constexpr int WQ_BYTES = KC * 96 * 128;     // one head's q|k|v weight rows
+  static constexpr int WO_BYTES = KC * DM * 128;     // Wo
+  static constexpr int WBUF = ((WQ_BYTES > WO_BYTES ? WQ_BYTES : WO_BYTES) + 1023) / 1024 * 1024;
+  static constexpr int A_BYTES = KC * 128 * 128;     // 128 token rows
+  static constexpr int K_BYTES = 128 * 64;           // 128 keys x 32 fp16, 64-byte swizzle
+  static constexpr int V_BYTES = 2 * 32 * 128;       // v^T: 32 x 128 keys, two 64-key atom columns
+  static constexpr int SLOT = 2 * A_BYTES + K_BYTES + V_BYTES;
+  static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + 1024;
+};
+
+enum FusedBar : int { FB_A_READY = 0, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY, FB_O_FULL,
+                      FB_CTX_READY, FB_OUT_FULL, FB_COUNT };
+
+template <int DM>
+__global__ void __launch_bounds__(384, 1)
+    fused_layer_kernel(const __grid_constant__ CUtensorMap map_wqkv, const __grid_constant__ CUtensorMap map_wo,
+                       FusedArgs a, DevStatus* status) {
+  using C = FusedCfg<DM>;
+  constexpr int H = C::H;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sSlot = smem + 2 * C::WBUF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSlot + 2 * C::SLOT);
+  uint64_t* w_full = bars;
+  uint64_t* w_empty = bars + 2;
+  uint64_t* mma_done = bars + 4 + 2 * FB_COUNT;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 2);
+  auto sb = [&](int s, int i) { return bars + 4 + FB_COUNT * s + i; };
+  auto slot_a = [&](int s) { return sSlot + s * C::SLOT; };
+  auto slot_c = [&](int s) { return sSlot + s * C::SLOT + C::A_BYTES; };
+  auto slot_k = [&](int s) { return sSlot + s * C::SLOT + 2 * C::A_BYTES; };
+  auto slot_v = [&](int s) { return sSlot + s * C::SLOT + 2 * C::A_BYTES + C::K_BYTES; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npairs = (a.B + 1) / 2;
+  const int S = a.S;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&w_full[i], 1);
+      mbar_init(&w_empty[i], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(sb(s, FB_A_READY), 4);
+      mbar_init(sb(s, FB_QKV_FULL), 1);
+      mbar_init(sb(s, FB_QKV_FREE), 4);
+      mbar_init(sb(s, FB_KQV_READY), 4);
+      mbar_init(sb(s, FB_S_FULL), 1);
+      mbar_init(sb(s, FB_P_READY), 4);
+      mbar_init(sb(s, FB_O_FULL), 1);
+      mbar_init(sb(s, FB_CTX_READY), 4);
+      mbar_init(sb(s, FB_OUT_FULL), 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_wqkv);
+    tma_prefetch_desc(&map_wo);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ======================= TMA producer: weight tiles
+      int wt = 0, last[2] = {-1, -1};
+      bool ok = true;
+      for (int pair = blockIdx.x; pair < npairs && ok; pair += gridDim.x) {
+        for (int t = 0; t <= H; ++t, ++wt) {
+          const int b = wt & 1;
+          if (!mbar_wait(&w_empty[b], ((wt >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* dst = sW + b * C::WBUF;
+          if (t < H) {
+            mbar_arrive_expect_tx(&w_full[b], C::WQ_BYTES);
+            for (int kc = 0; kc < C::KC; ++kc)
+              for (int part = 0; part < 3; ++part)
+                tma_load_2d(dst + kc * (96 * 128) + part * (32 * 128), &map_wqkv, &w_full[b], kc * 64,
+                            part * DM + t * 32);
+          } else {
+            mbar_arrive_expect_tx(&w_full[b], C::WO_BYTES);
+            for (int kc = 0; kc < C::KC; ++kc)
+              tma_load_2d(dst + kc * (DM * 128), &map_wo, &w_full[b], kc * 64, 0);
+          }
+          last[b] = wt;
+        }
+      }
+      for (int b = 0; b < 2; ++b)
+        if (last[b] >= 0) mbar_drain(&w_full[b], (last[b] >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ======================= MMA issuer
+      const uint32_t id_qkv = idesc_f16_f32(128, 96);
+      const uint32_t id_s = idesc_f16_f32(128, 128);
+      const uint32_t id_o = idesc_f16_f32(128, 32);
+      const uint32_t id_out = idesc_f16_f32(128, DM);
+      int wt = 0, pi = 0;
+      bool ok = true;
+      for (int pair = blockIdx.x; pair < npairs && ok; pair += gridDim.x, ++pi) {
+        const int ns = (2 * pair + 1 < a.B) ? 2 : 1;
+        for (int s = 0; s < ns && ok; ++s)
+          if (!mbar_wait(sb(s, FB_A_READY), pi & 1, abort_flag)) ok = false;
+        for (int h = 0; h < H && ok; ++h, ++wt) {
+          const int b = wt & 1;
+          const int n = pi * H + h;
+          if (!mbar_wait(&w_full[b], (wt >> 1) & 1, abort_flag)) { ok = false; break; }
+          const uint32_t wbase = smem_u32(sW + b * C::WBUF);
+          for (int s = 0; s < ns; ++s) {  // q|k|v of head h
+            if (n > 0 && !mbar_wait(sb(s, FB_QKV_FREE), (n - 1) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t abase = smem_u32(slot_a(s));
+#pragma unroll
+            for (int k = 0; k < DM / 16; ++k) {
+              const uint32_t oa = (uint32_t)(k >> 2) * 16384 + (k & 3) * 32;
+              const uint32_t ow = (uint32_t)(k >> 2) * (96 * 128) + (k & 3) * 32;
+              umma_f16_ss(tmem_base + s * 256, sdesc_kmajor(abase + oa, 128), sdesc_kmajor(wbase + ow, 128), id_qkv,
+                          k > 0 ? 1u : 0u);
+            }
+            umma_commit(sb(s, FB_QKV_FULL));
+          }
+          if (!ok) break;
+          umma_commit(&w_empty[b]);
+          for (int s = 0; s < ns; ++s) {  // S = q k^T, q from TMEM
+            if (!mbar_wait(sb(s, FB_KQV_READY), n & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t kbase = smem_u32(slot_k(s));
+            const uint32_t tq = tmem_base + s * 256 + 96;
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+              umma_f16_ts(tmem_base + s * 256 + 128, tq + k * 8, sdesc_kmajor(kbase + k * 32, 64), id_s,
+                          k > 0 ? 1u : 0u);
+            umma_commit(sb(s, FB_S_FULL));
+          }
+          if (!ok) break;
+          for (int s = 0; s < ns; ++s) {  // O = P v, P from TMEM
+            if (!mbar_wait(sb(s, FB_P_READY), n & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t vbase = smem_u32(slot_v(s));
+            const uint32_t tp = tmem_base + s * 256 + 128;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              umma_f16_ts(tmem_base + s * 256 + 96, tp + k * 8,
+                          sdesc_kmajor(vbase + (uint32_t)(k >> 2) * 4096 + (k & 3) * 32, 128), id_o,
+                          k > 0 ? 1u : 0u);
+            umma_commit(sb(s, FB_O_FULL));
+          }
+        }
+        if (!ok) break;
+        {  // out-projection: ctx Wo^T
+          const int b = wt & 1;
+          if (!mbar_wait(&w_full[b], (wt >> 1) & 1, abort_flag)) { ok = false; break; }
+          const uint32_t wbase = smem_u32(sW + b * C::WBUF);
+          for (int s = 0; s < ns; ++s) {
+            if (!mbar_wait(sb(s, FB_CTX_READY), pi & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t cbase = smem_u32(slot_c(s));
+#pragma unroll
+            for (int k = 0; k < DM / 16; ++k) {
+              const uint32_t oc = (uint32_t)(k >> 2) * 16384 + (k & 3) * 32;
+              const uint32_t ow = (uint32_t)(k >> 2) * (DM * 128) + (k & 3) * 32;
+              umma_f16_ss(tmem_base + s * 256, sdesc_kmajor(cbase + oc, 128), sdesc_kmajor(wbase + ow, 128), id_out,
+                          k > 0 ? 1u : 0u);
+            }
+            umma_commit(sb(s, FB_OUT_FULL));
+          }
+          if (!ok) break;
+          umma_commit(&w_empty[b]);
+          ++wt;
+        }
+      }
+      umma_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+  } else if (warp >= 4) {  // ======================= row workers, one token per thread
+    const int s = (warp - 4) >> 2;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t tb = tmem_base + (uint32_t)(s * 256) + ((uint32_t)(q * 32) << 16);
+    const uint32_t a_base = smem_u32(slot_a(s));
+    const uint32_t c_base = smem_u32(slot_c(s));
+    const uint32_t k_base = smem_u32(slot_k(s));
+    const uint32_t v_base = smem_u32(slot_v(s));
+    const float sl2 = a.scale_log2;
+    const float inv_d = 1.0f / (float)DM;
+    int pi = 0;
+    for (int pair = blockIdx.x; pair < npairs; pair += gridDim.x, ++pi) {
+      const int seq = 2 * pair + s;
+      if (seq >= a.B) break;
+      const long long t0 = (long long)seq * S;
+      {  // pull the next sequence of this slot toward L2
+        const int nseq = seq + 2 * (int)gridDim.x;
+        if (nseq < a.B && row < S) {
+          const char* p = reinterpret_cast<const char*>(a.x + ((long long)nseq * S + row) * DM);
+#pragma unroll
+          for (int i = 0; i < DM * 4 / 128; ++i) prefetch_l2(p + i * 128);
+        }
+      }
+      // ---- LN1: warp q normalises rows q*32 .. q*32+31 (one row per step, coalesced)
+#pragma unroll 1
+      for (int rr = 0; rr < 32; ++rr) {
+        const int r = q * 32 + rr;
+        const int k = lane * 4;
+        const bool valid = r < S && k < DM;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) v = __ldg(reinterpret_cast<const float4*>(a.x + (t0 + r) * DM + k));
+        const float mean = warp_sum((v.x + v.y) + (v.z + v.w)) * inv_d;
+        float sq = 0.f;
+        if (k < DM) {
+          const float e0 = v.x - mean, e1 = v.y - mean, e2 = v.z - mean, e3 = v.w - mean;
+          sq = (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
+        }
+        const float rstd = rsqrtf(warp_sum(sq) * inv_d + a.eps1);
+        if (k < DM) {
+          uint32_t lo = 0, hi = 0;
+          if (valid) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4*>(a.ln1_w + k));
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(a.ln1_b + k));
+            lo = pack_half2((v.x - mean) * rstd * w4.x + b4.x, (v.y - mean) * rstd * w4.y + b4.y);
+            hi = pack_half2((v.z - mean) * rstd * w4.z + b4.z, (v.w - mean) * rstd * w4.w + b4.w);
+          }
+          st_shared_v2(a_base + (k >> 6) * 16384 + swz_offset(r, (k & 63) >> 3, 128) + (k & 7) * 2, lo, hi);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sb(s, FB_A_READY));
+
+      bool ok = true;
+      for (int h = 0; h < H; ++h) {
+        const int n = pi * H + h;
+        // ---- q|k|v of head h: bias, fp16; q -> TMEM, k and v^T -> shared memory
+        if (!mbar_wait(sb(s, FB_QKV_FULL), n & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        {
+          uint32_t r[32], pk[16];
+          tmem_ld32(tb + 0, r);
+          const float4* bq = reinterpret_cast<const float4*>(a.bqkv + 32 * h);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(bq + i);
+            pk[2 * i] = pack_half2(__uint_as_float(r[4 * i]) + bb.x, __uint_as_float(r[4 * i + 1]) + bb.y);
+            pk[2 * i + 1] = pack_half2(__uint_as_float(r[4 * i + 2]) + bb.z, __uint_as_float(r[4 * i + 3]) + bb.w);
+          }
+          tmem_st16(tb + 96, pk);
+          tmem_ld32(tb + 32, r);
+          const float4* bk = reinterpret_cast<const float4*>(a.bqkv + DM + 32 * h);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(bk + i);
+            pk[2 * i] = pack_half2(__uint_as_float(r[4 * i]) + bb.x, __uint_as_float(r[4 * i + 1]) + bb.y);
+            pk[2 * i + 1] = pack_half2(__uint_as_float(r[4 * i + 2]) + bb.z, __uint_as_float(r[4 * i + 3]) + bb.w);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            st_shared_v4(k_base + row * 64 + ((c ^ ((row >> 1) & 3)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                         pk[4 * c + 3]);
+          tmem_ld32(tb + 64, r);
+          const float4* bv = reinterpret_cast<const float4*>(a.bqkv + 2 * DM + 32 * h);
+          const uint32_t vrow = v_base + (uint32_t)(row >> 6) * 4096 + (row & 7) * 2;
+          const int vch = (row & 63) >> 3;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(bv + i);
+            const float vv[4] = {__uint_as_float(r[4 * i]) + bb.x, __uint_as_float(r[4 * i + 1]) + bb.y,
+                                 __uint_as_float(r[4 * i + 2]) + bb.z, __uint_as_float(r[4 * i + 3]) + bb.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = 4 * i + e;
+              st_shared_u16(vrow + j * 128 + ((vch ^ (j & 7)) << 4), __half_as_ushort(__float2half_rn(vv[e])));
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (h < H - 1) mbar_arrive(sb(s, FB_QKV_FREE));
+          mbar_arrive(sb(s, FB_KQV_READY));
+        }
+        // ---- softmax of S = q k^T (one row per thread, exact: S <= 128 keys)
+        if (!mbar_wait(sb(s, FB_S_FULL), n & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const int lim = a.causal ? min(S, row + 1) : S;  // keys [0, lim) are visible
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tb + 128 + 32 * c, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (32 * c + i < lim) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
+        const float ms = mx * sl2;
+        float l = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32], pk[16];
+          tmem_ld32(tb + 128 + 32 * c, r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k0 = 32 * c + 2 * i;
+            const float p0 = (k0 < lim) ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), sl2, -ms)) : 0.f;
+            const float p1 = (k0 + 1 < lim) ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -ms)) : 0.f;
+            l += p0 + p1;
+            pk[i] = pack_half2(p0, p1);
+          }
+          tmem_st16(tb + 128 + 16 * c, pk);  // P overwrites the S columns already read
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sb(s, FB_P_READY));
+        // ---- ctx columns of head h = O / l, fp16, into the out-projection operand
+        if (!mbar_wait(sb(s, FB_O_FULL), n & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        {
+          uint32_t r[32];
+          tmem_ld32(tb + 96, r);
+          const float il = 1.0f / l;
+          const int col0 = 32 * h;
+          const uint32_t cb = c_base + (uint32_t)(col0 >> 6) * 16384 + row * 128;
+          const int ch0 = (col0 & 63) >> 3;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            st_shared_v4(cb + (((ch0 + c) ^ (row & 7)) << 4),
+                         pack_half2(__uint_as_float(r[8 * c + 0]) * il, __uint_as_float(r[8 * c + 1]) * il),
+                         pack_half2(__uint_as_float(r[8 * c + 2]) * il, __uint_as_float(r[8 * c + 3]) * il),
+                         pack_half2(__uint_as_float(r[8 * c + 4]) * il, __uint_as_float(r[8 * c + 5]) * il),
+                         pack_half2(__uint_as_float(r[8 * c + 6]) * il, __uint_as_float(r[8 * c + 7]) * il));
+        }
+      }
+      if (!ok) break;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sb(s, FB_CTX_READY));
+      // ---- out-projection epilogue: r = x + (acc + bo), LN2, y
+      if (!mbar_wait(sb(s, FB_OUT_FULL), pi & 1, abort_flag)) break;
+      tc_fence_after();
+      {
+        const bool valid = row < S;
+        const float* xr = a.x + (t0 + row) * DM;
+        float sum = 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < DM / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tb + 32 * cc, r);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int col = cc * 32 + 4 * c;
+            if (valid) {
+              const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + col));
+              const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bo + col));
+              const float a0 = xv.x + (__uint_as_float(r[4 * c + 0]) + bb.x);
+              const float a1 = xv.y + (__uint_as_float(r[4 * c + 1]) + bb.y);
+              const float a2 = xv.z + (__uint_as_float(r[4 * c + 2]) + bb.z);
+              const float a3 = xv.w + (__uint_as_float(r[4 * c + 3]) + bb.w);
+              sum += (a0 + a1) + (a2 + a3);
+              r[4 * c + 0] = __float_as_uint(a0);
+              r[4 * c + 1] = __float_as_uint(a1);
+              r[4 * c + 2] = __float_as_uint(a2);
+              r[4 * c + 3] = __float_as_uint(a3);
+            }
+          }
+          tmem_st32(tb + 32 * cc, r);
+        }
+        const float mean = sum * inv_d;
+        float sq = 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < DM / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tb + 32 * cc, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float dv = __uint_as_float(r[i]) - mean;
+            sq += dv * dv;
+          }
+        }
+        const float rstd = rsqrtf(sq * inv_d + a.eps2);
+#pragma unroll 1
+        for (int cc = 0; cc < DM / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tb + 32 * cc, r);
+          if (valid) {
+            float* yr = a.y + (t0 + row) * DM;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int col = cc * 32 + 4 * c;
+              const float4 wv = __ldg(reinterpret_cast<const float4*>(a.ln2_w + col));
+              const float4 bb = __ldg(reinterpret_cast<const float4*>(a.ln2_b + col));
+              float4 o;
+              o.x = (__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bb.x;
+              o.y = (__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bb.y;
+              o.z = (__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bb.z;
+              o.w = (__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bb.w;
+              *reinterpret_cast<float4*>(yr + col) = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sb(s, FB_QKV_FREE));  // TMEM [0, d) free for the next sequence
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kFusedLayer, 0);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace b200l

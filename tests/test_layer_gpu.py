@@ -246,3 +246,33 @@ def test_error_codes(pkg, cuda_ok):
     bad = pkg.B200TransformerLayer(48, 3).cuda()      # head_dim 16: unsupported
     with pytest.raises(pkg._lib.B200LError, match="head_dim 16 unsupported"):
         bad(torch.zeros(1, 4, 48, device="cuda"))
+
+
+FUSED_SHAPES = [
+    (4, 128, 128, 4, False),    # cfg1
+    (3, 128, 128, 4, False),    # odd batch: the last pair has one sequence
+    (5, 77, 128, 4, True),      # S < 128, causal
+    (1, 1, 128, 4, False),      # S = 1
+    (2, 100, 64, 2, False),     # d = 64
+    (300, 128, 128, 4, False),  # more pairs than SMs: persistent loop
+]
+
+
+@pytest.mark.parametrize("shape", FUSED_SHAPES, ids=_ids)
+def test_fused_layer_matches_three_kernel_path(pkg, cuda_ok, shape):
+    """b200l_layer_forward runs the whole-layer kernel for d in {64, 128},
+    head_dim 32, S <= 128; the per-kernel entry points run K1 -> K2 -> K3.
+    Both must pass the reference gate and agree with each other."""
+    B, S, d, H, causal = shape
+    cfg, ref, lay = make_layer(pkg, B, S, d, H, causal)
+    x, _ = generate_random_case(cfg, seed=4321)
+    xg = x.cuda()
+    with torch.inference_mode():
+        y3 = run_stepwise(pkg, lay, xg)
+        yf = lay(xg).clone()
+        torch.cuda.synchronize()
+        lay.check_status()
+        y_ref = ref(x)
+    _close("fused vs three-kernel", yf, y3, 1e-3, 1e-3)
+    res = compare_outputs(y_ref, yf.cpu())
+    assert res.passed, f"fused layer gate failed: {res}"
