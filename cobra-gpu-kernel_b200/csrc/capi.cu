@@ -113,7 +113,8 @@ EncodeTiledFn encode_fn() {
 // fp16 tensor of rank 2 or 3; dims/strides innermost first, strides in bytes
 // for dims 1.. ; box innermost first.
 int make_map(CUtensorMap* map, const void* base, int rank, const unsigned long long* dims,
-             const unsigned long long* strides_bytes, const unsigned* box, CUtensorMapSwizzle swz, const char* what) {
+             const unsigned long long* strides_bytes, const unsigned* box, CUtensorMapSwizzle swz, const char* what,
+             CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT16) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(B200L_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable from the driver");
   cuuint64_t gd[3], gs[2];
@@ -123,7 +124,7 @@ int make_map(CUtensorMap* map, const void* base, int rank, const unsigned long l
     bx[i] = box[i];
   }
   for (int i = 0; i + 1 < rank; ++i) gs[i] = strides_bytes[i];
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bx, es,
+  CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bx, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(B200L_ERR_LAUNCH, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", what, (int)r);
@@ -364,6 +365,15 @@ int launch_fused_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& d
   int rc = map_rows_k(&map_wqkv, desc->wqkv, 3ull * DM, DM, 32, "wqkv");
   if (rc) return rc;
   if ((rc = map_rows_k(&map_wo, desc->wo, (unsigned long long)DM, DM, DM, "wo"))) return rc;
+  CUtensorMap map_y;  // y viewed as [B][S][d] fp32: rows past S are clipped on store
+  {
+    const unsigned long long dims[3] = {(unsigned long long)DM, (unsigned long long)p.S, (unsigned long long)p.B};
+    const unsigned long long strides[2] = {(unsigned long long)DM * 4, (unsigned long long)p.S * DM * 4};
+    const unsigned box[3] = {32, 128, 1};
+    if ((rc = make_map(&map_y, y, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "y",
+                       CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return rc;
+  }
   FusedArgs a;
   a.x = x; a.y = y;
   a.ln1_w = desc->ln1_w; a.ln1_b = desc->ln1_b; a.eps1 = desc->eps1;
@@ -376,7 +386,7 @@ int launch_fused_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& d
   if ((rc = ensure_smem((const void*)kern, smem))) return rc;
   const int npairs = (p.B + 1) / 2;
   const int grid = npairs < dev.sms ? npairs : dev.sms;
-  kern<<<grid, 384, smem, st>>>(map_wqkv, map_wo, a, reinterpret_cast<DevStatus*>(ws));
+  kern<<<grid, 512, smem, st>>>(map_wqkv, map_wo, map_y, a, reinterpret_cast<DevStatus*>(ws));
   return check_launch("fused_layer_kernel");
 }
 

@@ -21,8 +21,11 @@
 // C = ctx fp16 (A operand of the out-projection), k [128 x 32] and v^T [32 x 128]
 // fp16 of the current head. Weight tiles (q|k|v rows of one head, then Wo)
 // stream from L2 through a 2-deep TMA ring shared by both slots.
-// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 4-7 slot-0 rows,
-// 8-11 slot-1 rows (one token row per thread).
+// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 4-7 slot-0 rows, 8-11
+// slot-1 rows (one token row per thread: q|k|v epilogue, softmax, ctx, LN2),
+// 12-15 LayerNorm-1 of each slot's next sequence (warp per row, 8 rows of
+// loads in flight), so x loads stay off the critical path. y leaves through
+// the ctx buffer with TMA stores (full 128-byte lines).
 #pragma once
 
 #include "common.cuh"
@@ -56,15 +59,16 @@ struct FusedCfg {
   static constexpr int V_BYTES = 2 * 32 * 128;       // v^T: 32 x 128 keys, two 64-key atom columns
   static constexpr int SLOT = 2 * A_BYTES + K_BYTES + V_BYTES;
   static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + 1024;
+  static_assert(4 + 2 * 10 + 3 <= 64, "barrier block fits in 512 bytes");
 };
 
-enum FusedBar : int { FB_A_READY = 0, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY, FB_O_FULL,
-                      FB_CTX_READY, FB_OUT_FULL, FB_COUNT };
+enum FusedBar : int { FB_A_READY = 0, FB_A_FREE, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY,
+                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_COUNT };
 
 template <int DM>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     fused_layer_kernel(const __grid_constant__ CUtensorMap map_wqkv, const __grid_constant__ CUtensorMap map_wo,
-                       FusedArgs a, DevStatus* status) {
+                       const __grid_constant__ CUtensorMap map_y, FusedArgs a, DevStatus* status) {
   using C = FusedCfg<DM>;
   constexpr int H = C::H;
   extern __shared__ uint8_t smem_raw[];
@@ -93,7 +97,8 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&w_empty[i], 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(sb(s, FB_A_READY), 4);
+      mbar_init(sb(s, FB_A_READY), 2);
+      mbar_init(sb(s, FB_A_FREE), 4);
       mbar_init(sb(s, FB_QKV_FULL), 1);
       mbar_init(sb(s, FB_QKV_FREE), 4);
       mbar_init(sb(s, FB_KQV_READY), 4);
@@ -108,6 +113,7 @@ __global__ void __launch_bounds__(384, 1)
     fence_barrier_init();
     tma_prefetch_desc(&map_wqkv);
     tma_prefetch_desc(&map_wo);
+    tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -151,30 +157,36 @@ __global__ void __launch_bounds__(384, 1)
       const uint32_t id_out = idesc_f16_f32(128, DM);
       int wt = 0, pi = 0;
       bool ok = true;
+      // q|k|v projection of head h for every active slot, from weight tile wt.
+      auto issue_qkv = [&](int h, int ns) -> bool {
+        const int b = wt & 1;
+        const int n = pi * H + h;
+        if (!mbar_wait(&w_full[b], (wt >> 1) & 1, abort_flag)) return false;
+        const uint32_t wbase = smem_u32(sW + b * C::WBUF);
+        for (int s = 0; s < ns; ++s) {
+          if (n > 0 && !mbar_wait(sb(s, FB_QKV_FREE), (n - 1) & 1, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t abase = smem_u32(slot_a(s));
+#pragma unroll
+          for (int k = 0; k < DM / 16; ++k) {
+            const uint32_t oa = (uint32_t)(k >> 2) * 16384 + (k & 3) * 32;
+            const uint32_t ow = (uint32_t)(k >> 2) * (96 * 128) + (k & 3) * 32;
+            umma_f16_ss(tmem_base + s * 256, sdesc_kmajor(abase + oa, 128), sdesc_kmajor(wbase + ow, 128), id_qkv,
+                        k > 0 ? 1u : 0u);
+          }
+          umma_commit(sb(s, FB_QKV_FULL));
+        }
+        umma_commit(&w_empty[b]);
+        ++wt;
+        return true;
+      };
       for (int pair = blockIdx.x; pair < npairs && ok; pair += gridDim.x, ++pi) {
         const int ns = (2 * pair + 1 < a.B) ? 2 : 1;
         for (int s = 0; s < ns && ok; ++s)
           if (!mbar_wait(sb(s, FB_A_READY), pi & 1, abort_flag)) ok = false;
-        for (int h = 0; h < H && ok; ++h, ++wt) {
-          const int b = wt & 1;
+        if (!ok || !issue_qkv(0, ns)) { ok = false; break; }
+        for (int h = 0; h < H && ok; ++h) {
           const int n = pi * H + h;
-          if (!mbar_wait(&w_full[b], (wt >> 1) & 1, abort_flag)) { ok = false; break; }
-          const uint32_t wbase = smem_u32(sW + b * C::WBUF);
-          for (int s = 0; s < ns; ++s) {  // q|k|v of head h
-            if (n > 0 && !mbar_wait(sb(s, FB_QKV_FREE), (n - 1) & 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t abase = smem_u32(slot_a(s));
-#pragma unroll
-            for (int k = 0; k < DM / 16; ++k) {
-              const uint32_t oa = (uint32_t)(k >> 2) * 16384 + (k & 3) * 32;
-              const uint32_t ow = (uint32_t)(k >> 2) * (96 * 128) + (k & 3) * 32;
-              umma_f16_ss(tmem_base + s * 256, sdesc_kmajor(abase + oa, 128), sdesc_kmajor(wbase + ow, 128), id_qkv,
-                          k > 0 ? 1u : 0u);
-            }
-            umma_commit(sb(s, FB_QKV_FULL));
-          }
-          if (!ok) break;
-          umma_commit(&w_empty[b]);
           for (int s = 0; s < ns; ++s) {  // S = q k^T, q from TMEM
             if (!mbar_wait(sb(s, FB_KQV_READY), n & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
@@ -187,6 +199,8 @@ __global__ void __launch_bounds__(384, 1)
             umma_commit(sb(s, FB_S_FULL));
           }
           if (!ok) break;
+          // next head's projection runs while this head's softmax does
+          if (h + 1 < H && !issue_qkv(h + 1, ns)) { ok = false; break; }
           for (int s = 0; s < ns; ++s) {  // O = P v, P from TMEM
             if (!mbar_wait(sb(s, FB_P_READY), n & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
@@ -226,12 +240,70 @@ __global__ void __launch_bounds__(384, 1)
       umma_commit(mma_done);
       mbar_drain(mma_done, 0);
     }
-  } else if (warp >= 4) {  // ======================= row workers, one token per thread
+  } else if (warp >= 12) {  // ======================= LN1: warps 12,13 -> slot 0; 14,15 -> slot 1
+    const int s = (warp - 12) >> 1;
+    const int rbeg = ((warp - 12) & 1) * 64;
+    const uint32_t a_base = smem_u32(slot_a(s));
+    const float inv_d = 1.0f / (float)DM;
+    const int k = lane * 4;
+    float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = w4;
+    if (k < DM) {
+      w4 = __ldg(reinterpret_cast<const float4*>(a.ln1_w + k));
+      b4 = __ldg(reinterpret_cast<const float4*>(a.ln1_b + k));
+    }
+    int pi = 0;
+    for (int pair = blockIdx.x; pair < npairs; pair += gridDim.x, ++pi) {
+      const int seq = 2 * pair + s;
+      if (seq >= a.B) break;
+      const long long t0 = (long long)seq * S;
+      {  // pull this slot's next sequence (these 64 rows) toward L2
+        const int nseq = seq + 2 * (int)gridDim.x;
+        if (nseq < a.B && rbeg < S) {
+          const int rows = min(64, S - rbeg);
+          const char* p = reinterpret_cast<const char*>(a.x + ((long long)nseq * S + rbeg) * DM);
+          const int lines = (rows * DM * 4 + 127) / 128;
+          for (int i = lane; i < lines; i += 32) prefetch_l2(p + (long long)i * 128);
+        }
+      }
+      // A of this slot is free once the previous sequence's last projection was read.
+      if (!mbar_wait(sb(s, FB_A_FREE), (pi & 1) ^ 1, abort_flag)) break;
+#pragma unroll 1
+      for (int r0 = rbeg; r0 < rbeg + 64; r0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (r0 + j < S && k < DM) v[j] = __ldg(reinterpret_cast<const float4*>(a.x + (t0 + r0 + j) * DM + k));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int r = r0 + j;
+          const float mean = warp_sum((v[j].x + v[j].y) + (v[j].z + v[j].w)) * inv_d;
+          float sq = 0.f;
+          if (k < DM) {
+            const float e0 = v[j].x - mean, e1 = v[j].y - mean, e2 = v[j].z - mean, e3 = v[j].w - mean;
+            sq = (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
+          }
+          const float rstd = rsqrtf(warp_sum(sq) * inv_d + a.eps1);
+          if (k < DM) {
+            uint32_t lo = 0, hi = 0;
+            if (r < S) {
+              lo = pack_half2((v[j].x - mean) * rstd * w4.x + b4.x, (v[j].y - mean) * rstd * w4.y + b4.y);
+              hi = pack_half2((v[j].z - mean) * rstd * w4.z + b4.z, (v[j].w - mean) * rstd * w4.w + b4.w);
+            }
+            st_shared_v2(a_base + (k >> 6) * 16384 + swz_offset(r, (k & 63) >> 3, 128) + (k & 7) * 2, lo, hi);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sb(s, FB_A_READY));
+    }
+  } else if (warp >= 4) {  // ======================= row workers (warps 4-11), one token per thread
     const int s = (warp - 4) >> 2;
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t tb = tmem_base + (uint32_t)(s * 256) + ((uint32_t)(q * 32) << 16);
-    const uint32_t a_base = smem_u32(slot_a(s));
     const uint32_t c_base = smem_u32(slot_c(s));
     const uint32_t k_base = smem_u32(slot_k(s));
     const uint32_t v_base = smem_u32(slot_v(s));
@@ -242,44 +314,6 @@ __global__ void __launch_bounds__(384, 1)
       const int seq = 2 * pair + s;
       if (seq >= a.B) break;
       const long long t0 = (long long)seq * S;
-      {  // pull the next sequence of this slot toward L2
-        const int nseq = seq + 2 * (int)gridDim.x;
-        if (nseq < a.B && row < S) {
-          const char* p = reinterpret_cast<const char*>(a.x + ((long long)nseq * S + row) * DM);
-#pragma unroll
-          for (int i = 0; i < DM * 4 / 128; ++i) prefetch_l2(p + i * 128);
-        }
-      }
-      // ---- LN1: warp q normalises rows q*32 .. q*32+31 (one row per step, coalesced)
-#pragma unroll 1
-      for (int rr = 0; rr < 32; ++rr) {
-        const int r = q * 32 + rr;
-        const int k = lane * 4;
-        const bool valid = r < S && k < DM;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid) v = __ldg(reinterpret_cast<const float4*>(a.x + (t0 + r) * DM + k));
-        const float mean = warp_sum((v.x + v.y) + (v.z + v.w)) * inv_d;
-        float sq = 0.f;
-        if (k < DM) {
-          const float e0 = v.x - mean, e1 = v.y - mean, e2 = v.z - mean, e3 = v.w - mean;
-          sq = (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
-        }
-        const float rstd = rsqrtf(warp_sum(sq) * inv_d + a.eps1);
-        if (k < DM) {
-          uint32_t lo = 0, hi = 0;
-          if (valid) {
-            const float4 w4 = __ldg(reinterpret_cast<const float4*>(a.ln1_w + k));
-            const float4 b4 = __ldg(reinterpret_cast<const float4*>(a.ln1_b + k));
-            lo = pack_half2((v.x - mean) * rstd * w4.x + b4.x, (v.y - mean) * rstd * w4.y + b4.y);
-            hi = pack_half2((v.z - mean) * rstd * w4.z + b4.z, (v.w - mean) * rstd * w4.w + b4.w);
-          }
-          st_shared_v2(a_base + (k >> 6) * 16384 + swz_offset(r, (k & 63) >> 3, 128) + (k & 7) * 2, lo, hi);
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sb(s, FB_A_READY));
-
       bool ok = true;
       for (int h = 0; h < H; ++h) {
         const int n = pi * H + h;
@@ -330,20 +364,26 @@ __global__ void __launch_bounds__(384, 1)
         __syncwarp();
         if (lane == 0) {
           if (h < H - 1) mbar_arrive(sb(s, FB_QKV_FREE));
+          else mbar_arrive(sb(s, FB_A_FREE));   // last projection of this sequence has read A
           mbar_arrive(sb(s, FB_KQV_READY));
         }
         // ---- softmax of S = q k^T (one row per thread, exact: S <= 128 keys)
         if (!mbar_wait(sb(s, FB_S_FULL), n & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const int lim = a.causal ? min(S, row + 1) : S;  // keys [0, lim) are visible
+        const bool full = (lim == 128);
         float mx = -INFINITY;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
           tmem_ld32(tb + 128 + 32 * c, r);
+          if (full) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (32 * c + i < lim) mx = fmaxf(mx, __uint_as_float(r[i]));
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, (32 * c + i < lim) ? __uint_as_float(r[i]) : -INFINITY);
+          }
         }
         const float ms = mx * sl2;
         float l = 0.f;
@@ -354,8 +394,11 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int k0 = 32 * c + 2 * i;
-            const float p0 = (k0 < lim) ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), sl2, -ms)) : 0.f;
-            const float p1 = (k0 + 1 < lim) ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -ms)) : 0.f;
+            // masked keys: exp2(-inf) = 0
+            const float s0 = (full || k0 < lim) ? __uint_as_float(r[2 * i]) : -INFINITY;
+            const float s1 = (full || k0 + 1 < lim) ? __uint_as_float(r[2 * i + 1]) : -INFINITY;
+            const float p0 = ex2_approx(fmaf(s0, sl2, -ms));
+            const float p1 = ex2_approx(fmaf(s1, sl2, -ms));
             l += p0 + p1;
             pk[i] = pack_half2(p0, p1);
           }
@@ -389,32 +432,42 @@ __global__ void __launch_bounds__(384, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(sb(s, FB_CTX_READY));
       // ---- out-projection epilogue: r = x + (acc + bo), LN2, y
+      const bool valid = row < S;
+      const float* xr = a.x + (t0 + row) * DM;
+      float4 xn[8];   // residual row, one 32-column chunk ahead of its use
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        xn[c] = valid ? __ldg(reinterpret_cast<const float4*>(xr + 4 * c)) : make_float4(0.f, 0.f, 0.f, 0.f);
       if (!mbar_wait(sb(s, FB_OUT_FULL), pi & 1, abort_flag)) break;
       tc_fence_after();
       {
-        const bool valid = row < S;
-        const float* xr = a.x + (t0 + row) * DM;
         float sum = 0.f;
 #pragma unroll 1
         for (int cc = 0; cc < DM / 32; ++cc) {
+          float4 xc[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) xc[c] = xn[c];
+          if (cc + 1 < DM / 32) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              xn[c] = valid ? __ldg(reinterpret_cast<const float4*>(xr + (cc + 1) * 32 + 4 * c))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
           uint32_t r[32];
           tmem_ld32(tb + 32 * cc, r);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const int col = cc * 32 + 4 * c;
-            if (valid) {
-              const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + col));
-              const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bo + col));
-              const float a0 = xv.x + (__uint_as_float(r[4 * c + 0]) + bb.x);
-              const float a1 = xv.y + (__uint_as_float(r[4 * c + 1]) + bb.y);
-              const float a2 = xv.z + (__uint_as_float(r[4 * c + 2]) + bb.z);
-              const float a3 = xv.w + (__uint_as_float(r[4 * c + 3]) + bb.w);
-              sum += (a0 + a1) + (a2 + a3);
-              r[4 * c + 0] = __float_as_uint(a0);
-              r[4 * c + 1] = __float_as_uint(a1);
-              r[4 * c + 2] = __float_as_uint(a2);
-              r[4 * c + 3] = __float_as_uint(a3);
-            }
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bo + col));
+            const float a0 = xc[c].x + (__uint_as_float(r[4 * c + 0]) + bb.x);
+            const float a1 = xc[c].y + (__uint_as_float(r[4 * c + 1]) + bb.y);
+            const float a2 = xc[c].z + (__uint_as_float(r[4 * c + 2]) + bb.z);
+            const float a3 = xc[c].w + (__uint_as_float(r[4 * c + 3]) + bb.w);
+            sum += (a0 + a1) + (a2 + a3);
+            r[4 * c + 0] = __float_as_uint(a0);
+            r[4 * c + 1] = __float_as_uint(a1);
+            r[4 * c + 2] = __float_as_uint(a2);
+            r[4 * c + 3] = __float_as_uint(a3);
           }
           tmem_st32(tb + 32 * cc, r);
         }
@@ -431,31 +484,50 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         const float rstd = rsqrtf(sq * inv_d + a.eps2);
+        // y leaves through the (now free) ctx buffer: 32-column fp32 atoms in the
+        // 128-byte swizzled layout, stored by TMA (rows >= S are clipped).
+        constexpr int ATOMS_PER_ROUND = C::A_BYTES / 16384;   // 2 for d=128, 1 for d=64
+        constexpr int ROUNDS = (DM / 32) / ATOMS_PER_ROUND;
+        const uint8_t* cbuf = slot_c(s);
+        const bool leader = (q == 0 && lane == 0);
 #pragma unroll 1
-        for (int cc = 0; cc < DM / 32; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(tb + 32 * cc, r);
-          if (valid) {
-            float* yr = a.y + (t0 + row) * DM;
+        for (int rd = 0; rd < ROUNDS; ++rd) {
+#pragma unroll 1
+          for (int j = 0; j < ATOMS_PER_ROUND; ++j) {
+            const int cc = rd * ATOMS_PER_ROUND + j;
+            uint32_t r[32];
+            tmem_ld32(tb + 32 * cc, r);
+            const uint32_t dst = c_base + (uint32_t)j * 16384 + row * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               const int col = cc * 32 + 4 * c;
               const float4 wv = __ldg(reinterpret_cast<const float4*>(a.ln2_w + col));
               const float4 bb = __ldg(reinterpret_cast<const float4*>(a.ln2_b + col));
-              float4 o;
-              o.x = (__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bb.x;
-              o.y = (__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bb.y;
-              o.z = (__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bb.z;
-              o.w = (__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bb.w;
-              *reinterpret_cast<float4*>(yr + col) = o;
+              st_shared_v4(dst + ((c ^ (row & 7)) << 4),
+                           __float_as_uint((__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bb.x),
+                           __float_as_uint((__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bb.y),
+                           __float_as_uint((__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bb.z),
+                           __float_as_uint((__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bb.w));
             }
           }
+          fence_proxy_async_smem();
+          named_bar_sync(1 + s, 128);
+          if (leader) {
+            for (int j = 0; j < ATOMS_PER_ROUND; ++j)
+              tma_store_3d(&map_y, cbuf + j * 16384, (rd * ATOMS_PER_ROUND + j) * 32, 0, seq);
+            bulk_commit();
+            bulk_wait_read_all();   // the buffer may be rewritten once TMA has read it
+          }
+          named_bar_sync(1 + s, 128);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(sb(s, FB_QKV_FREE));  // TMEM [0, d) free for the next sequence
     }
+  }
+  if (warp == 4 || warp == 8) {
+    if (lane == 0) bulk_wait_all();
   }
   __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kFusedLayer, 0);
