@@ -365,11 +365,16 @@ int launch_fused_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& d
   int rc = map_rows_k(&map_wqkv, desc->wqkv, 3ull * DM, DM, 32, "wqkv");
   if (rc) return rc;
   if ((rc = map_rows_k(&map_wo, desc->wo, (unsigned long long)DM, DM, DM, "wo"))) return rc;
-  CUtensorMap map_y;  // y viewed as [B][S][d] fp32: rows past S are clipped on store
+  // x and y viewed as [B][S][d] fp32 in 128-row x 32-column boxes: rows past S
+  // read as zero and are clipped on store.
+  CUtensorMap map_x, map_y;
   {
     const unsigned long long dims[3] = {(unsigned long long)DM, (unsigned long long)p.S, (unsigned long long)p.B};
     const unsigned long long strides[2] = {(unsigned long long)DM * 4, (unsigned long long)p.S * DM * 4};
     const unsigned box[3] = {32, 128, 1};
+    if ((rc = make_map(&map_x, x, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "x",
+                       CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return rc;
     if ((rc = make_map(&map_y, y, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "y",
                        CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
       return rc;
@@ -386,7 +391,7 @@ int launch_fused_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& d
   if ((rc = ensure_smem((const void*)kern, smem))) return rc;
   const int npairs = (p.B + 1) / 2;
   const int grid = npairs < dev.sms ? npairs : dev.sms;
-  kern<<<grid, 512, smem, st>>>(map_wqkv, map_wo, map_y, a, reinterpret_cast<DevStatus*>(ws));
+  kern<<<grid, 512, smem, st>>>(map_wqkv, map_wo, map_x, map_y, a, reinterpret_cast<DevStatus*>(ws));
   return check_launch("fused_layer_kernel");
 }
 

@@ -21,11 +21,13 @@
 // C = ctx fp16 (A operand of the out-projection), k [128 x 32] and v^T [32 x 128]
 // fp16 of the current head. Weight tiles (q|k|v rows of one head, then Wo)
 // stream from L2 through a 2-deep TMA ring shared by both slots.
-// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 4-7 slot-0 rows, 8-11
+// Warps: 0 TMA producer, 1 / 2 MMA issuers of slot 0 / 1 (warp 1 owns TMEM;
+// separate issuers keep one slot from stalling the other), 4-7 slot-0 rows, 8-11
 // slot-1 rows (one token row per thread: q|k|v epilogue, softmax, ctx, LN2),
-// 12-15 LayerNorm-1 of each slot's next sequence (warp per row, 8 rows of
-// loads in flight), so x loads stay off the critical path. y leaves through
-// the ctx buffer with TMA stores (full 128-byte lines).
+// 12-15 LayerNorm-1 of each slot's next sequence (warp per row, 16 rows of
+// loads in flight), so x loads stay off the critical path. In the LN2
+// epilogue the residual x arrives by TMA in 32-column chunks through the free
+// k|v buffer and y leaves by TMA stores, so both move as full 128-byte lines.
 #pragma once
 
 #include "common.cuh"
@@ -59,16 +61,18 @@ struct FusedCfg {
   static constexpr int V_BYTES = 2 * 32 * 128;       // v^T: 32 x 128 keys, two 64-key atom columns
   static constexpr int SLOT = 2 * A_BYTES + K_BYTES + V_BYTES;
   static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + 1024;
-  static_assert(4 + 2 * 10 + 3 <= 64, "barrier block fits in 512 bytes");
+  static_assert(4 + 2 * 13 + 3 <= 64, "barrier block fits in 512 bytes");
+  static_assert(K_BYTES + V_BYTES == 16384, "k|v buffer holds one 32-column fp32 chunk of x");
 };
 
 enum FusedBar : int { FB_A_READY = 0, FB_A_FREE, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY,
-                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_COUNT };
+                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_X0, FB_X1, FB_X2, FB_COUNT };
 
 template <int DM>
 __global__ void __launch_bounds__(512, 1)
     fused_layer_kernel(const __grid_constant__ CUtensorMap map_wqkv, const __grid_constant__ CUtensorMap map_wo,
-                       const __grid_constant__ CUtensorMap map_y, FusedArgs a, DevStatus* status) {
+                       const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_y,
+                       FusedArgs a, DevStatus* status) {
   using C = FusedCfg<DM>;
   constexpr int H = C::H;
   extern __shared__ uint8_t smem_raw[];
@@ -94,7 +98,7 @@ __global__ void __launch_bounds__(512, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&w_full[i], 1);
-      mbar_init(&w_empty[i], 1);
+      mbar_init(&w_empty[i], 2);   // released by both slots' MMA threads
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(sb(s, FB_A_READY), 2);
@@ -107,12 +111,16 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(sb(s, FB_O_FULL), 1);
       mbar_init(sb(s, FB_CTX_READY), 4);
       mbar_init(sb(s, FB_OUT_FULL), 1);
+      mbar_init(sb(s, FB_X0), 1);
+      mbar_init(sb(s, FB_X1), 1);
+      mbar_init(sb(s, FB_X2), 1);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&map_wqkv);
     tma_prefetch_desc(&map_wo);
+    tma_prefetch_desc(&map_x);
     tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
@@ -149,29 +157,35 @@ __global__ void __launch_bounds__(512, 1)
       for (int b = 0; b < 2; ++b)
         if (last[b] >= 0) mbar_drain(&w_full[b], (last[b] >> 1) & 1);
     }
-  } else if (warp == 1) {
-    if (lane == 0) {  // ======================= MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    if (lane == 0) {  // ======================= MMA issuer of slot (warp - 1)
+      const int s = warp - 1;
       const uint32_t id_qkv = idesc_f16_f32(128, 96);
       const uint32_t id_s = idesc_f16_f32(128, 128);
       const uint32_t id_o = idesc_f16_f32(128, 32);
       const uint32_t id_out = idesc_f16_f32(128, DM);
+      const uint32_t t_slot = tmem_base + s * 256;
+      const uint32_t abase = smem_u32(slot_a(s));
+      const uint32_t cbase = smem_u32(slot_c(s));
+      const uint32_t kbase = smem_u32(slot_k(s));
+      const uint32_t vbase = smem_u32(slot_v(s));
       int wt = 0, pi = 0;
       bool ok = true;
-      // q|k|v projection of head h for every active slot, from weight tile wt.
-      auto issue_qkv = [&](int h, int ns) -> bool {
+      // q|k|v projection of head h from weight tile wt; both slots' issuers
+      // read the same tile and each releases it once its MMAs finish.
+      auto issue_qkv = [&](int h, bool active) -> bool {
         const int b = wt & 1;
         const int n = pi * H + h;
         if (!mbar_wait(&w_full[b], (wt >> 1) & 1, abort_flag)) return false;
-        const uint32_t wbase = smem_u32(sW + b * C::WBUF);
-        for (int s = 0; s < ns; ++s) {
+        if (active) {
           if (n > 0 && !mbar_wait(sb(s, FB_QKV_FREE), (n - 1) & 1, abort_flag)) return false;
           tc_fence_after();
-          const uint32_t abase = smem_u32(slot_a(s));
+          const uint32_t wbase = smem_u32(sW + b * C::WBUF);
 #pragma unroll
           for (int k = 0; k < DM / 16; ++k) {
             const uint32_t oa = (uint32_t)(k >> 2) * 16384 + (k & 3) * 32;
             const uint32_t ow = (uint32_t)(k >> 2) * (96 * 128) + (k & 3) * 32;
-            umma_f16_ss(tmem_base + s * 256, sdesc_kmajor(abase + oa, 128), sdesc_kmajor(wbase + ow, 128), id_qkv,
+            umma_f16_ss(t_slot, sdesc_kmajor(abase + oa, 128), sdesc_kmajor(wbase + ow, 128), id_qkv,
                         k > 0 ? 1u : 0u);
           }
           umma_commit(sb(s, FB_QKV_FULL));
@@ -181,34 +195,29 @@ __global__ void __launch_bounds__(512, 1)
         return true;
       };
       for (int pair = blockIdx.x; pair < npairs && ok; pair += gridDim.x, ++pi) {
-        const int ns = (2 * pair + 1 < a.B) ? 2 : 1;
-        for (int s = 0; s < ns && ok; ++s)
-          if (!mbar_wait(sb(s, FB_A_READY), pi & 1, abort_flag)) ok = false;
-        if (!ok || !issue_qkv(0, ns)) { ok = false; break; }
+        // slot 1 may be empty in the last pair: it still walks the weight ring
+        const bool active = 2 * pair + s < a.B;
+        if (active && !mbar_wait(sb(s, FB_A_READY), pi & 1, abort_flag)) { ok = false; break; }
+        if (!issue_qkv(0, active)) { ok = false; break; }
         for (int h = 0; h < H && ok; ++h) {
           const int n = pi * H + h;
-          for (int s = 0; s < ns; ++s) {  // S = q k^T, q from TMEM
+          if (active) {  // S = q k^T, q from TMEM
             if (!mbar_wait(sb(s, FB_KQV_READY), n & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t kbase = smem_u32(slot_k(s));
-            const uint32_t tq = tmem_base + s * 256 + 96;
 #pragma unroll
             for (int k = 0; k < 2; ++k)
-              umma_f16_ts(tmem_base + s * 256 + 128, tq + k * 8, sdesc_kmajor(kbase + k * 32, 64), id_s,
+              umma_f16_ts(t_slot + 128, t_slot + 96 + k * 8, sdesc_kmajor(kbase + k * 32, 64), id_s,
                           k > 0 ? 1u : 0u);
             umma_commit(sb(s, FB_S_FULL));
           }
-          if (!ok) break;
           // next head's projection runs while this head's softmax does
-          if (h + 1 < H && !issue_qkv(h + 1, ns)) { ok = false; break; }
-          for (int s = 0; s < ns; ++s) {  // O = P v, P from TMEM
+          if (h + 1 < H && !issue_qkv(h + 1, active)) { ok = false; break; }
+          if (active) {  // O = P v, P from TMEM
             if (!mbar_wait(sb(s, FB_P_READY), n & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t vbase = smem_u32(slot_v(s));
-            const uint32_t tp = tmem_base + s * 256 + 128;
 #pragma unroll
             for (int k = 0; k < 8; ++k)
-              umma_f16_ts(tmem_base + s * 256 + 96, tp + k * 8,
+              umma_f16_ts(t_slot + 96, t_slot + 128 + k * 8,
                           sdesc_kmajor(vbase + (uint32_t)(k >> 2) * 4096 + (k & 3) * 32, 128), id_o,
                           k > 0 ? 1u : 0u);
             umma_commit(sb(s, FB_O_FULL));
@@ -218,21 +227,19 @@ __global__ void __launch_bounds__(512, 1)
         {  // out-projection: ctx Wo^T
           const int b = wt & 1;
           if (!mbar_wait(&w_full[b], (wt >> 1) & 1, abort_flag)) { ok = false; break; }
-          const uint32_t wbase = smem_u32(sW + b * C::WBUF);
-          for (int s = 0; s < ns; ++s) {
+          if (active) {
             if (!mbar_wait(sb(s, FB_CTX_READY), pi & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t cbase = smem_u32(slot_c(s));
+            const uint32_t wbase = smem_u32(sW + b * C::WBUF);
 #pragma unroll
             for (int k = 0; k < DM / 16; ++k) {
               const uint32_t oc = (uint32_t)(k >> 2) * 16384 + (k & 3) * 32;
               const uint32_t ow = (uint32_t)(k >> 2) * (DM * 128) + (k & 3) * 32;
-              umma_f16_ss(tmem_base + s * 256, sdesc_kmajor(cbase + oc, 128), sdesc_kmajor(wbase + ow, 128), id_out,
+              umma_f16_ss(t_slot, sdesc_kmajor(cbase + oc, 128), sdesc_kmajor(wbase + ow, 128), id_out,
                           k > 0 ? 1u : 0u);
             }
             umma_commit(sb(s, FB_OUT_FULL));
           }
-          if (!ok) break;
           umma_commit(&w_empty[b]);
           ++wt;
         }
@@ -267,29 +274,48 @@ __global__ void __launch_bounds__(512, 1)
       }
       // A of this slot is free once the previous sequence's last projection was read.
       if (!mbar_wait(sb(s, FB_A_FREE), (pi & 1) ^ 1, abort_flag)) break;
+      constexpr int LNB = 16;   // rows per batch: 16 coalesced row loads in flight per warp
 #pragma unroll 1
-      for (int r0 = rbeg; r0 < rbeg + 64; r0 += 8) {
-        float4 v[8];
+      for (int r0 = rbeg; r0 < rbeg + 64; r0 += LNB) {
+        float4 v[LNB];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < LNB; ++j) {
           v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
           if (r0 + j < S && k < DM) v[j] = __ldg(reinterpret_cast<const float4*>(a.x + (t0 + r0 + j) * DM + k));
         }
+        // LNB rows reduced together: each xor-shuffle step has LNB independent
+        // shuffles in flight instead of one dependent chain per row.
+        float red[LNB];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int r = r0 + j;
-          const float mean = warp_sum((v[j].x + v[j].y) + (v[j].z + v[j].w)) * inv_d;
+        for (int j = 0; j < LNB; ++j) red[j] = (v[j].x + v[j].y) + (v[j].z + v[j].w);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int j = 0; j < LNB; ++j) red[j] += __shfl_xor_sync(0xffffffffu, red[j], o);
+        float mean[LNB];
+#pragma unroll
+        for (int j = 0; j < LNB; ++j) {
+          mean[j] = red[j] * inv_d;
           float sq = 0.f;
           if (k < DM) {
-            const float e0 = v[j].x - mean, e1 = v[j].y - mean, e2 = v[j].z - mean, e3 = v[j].w - mean;
+            const float e0 = v[j].x - mean[j], e1 = v[j].y - mean[j], e2 = v[j].z - mean[j], e3 = v[j].w - mean[j];
             sq = (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
           }
-          const float rstd = rsqrtf(warp_sum(sq) * inv_d + a.eps1);
+          red[j] = sq;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int j = 0; j < LNB; ++j) red[j] += __shfl_xor_sync(0xffffffffu, red[j], o);
+#pragma unroll
+        for (int j = 0; j < LNB; ++j) {
+          const int r = r0 + j;
+          const float rstd = rsqrtf(red[j] * inv_d + a.eps1);
           if (k < DM) {
             uint32_t lo = 0, hi = 0;
             if (r < S) {
-              lo = pack_half2((v[j].x - mean) * rstd * w4.x + b4.x, (v[j].y - mean) * rstd * w4.y + b4.y);
-              hi = pack_half2((v[j].z - mean) * rstd * w4.z + b4.z, (v[j].w - mean) * rstd * w4.w + b4.w);
+              lo = pack_half2((v[j].x - mean[j]) * rstd * w4.x + b4.x, (v[j].y - mean[j]) * rstd * w4.y + b4.y);
+              hi = pack_half2((v[j].z - mean[j]) * rstd * w4.z + b4.z, (v[j].w - mean[j]) * rstd * w4.w + b4.w);
             }
             st_shared_v2(a_base + (k >> 6) * 16384 + swz_offset(r, (k & 63) >> 3, 128) + (k & 7) * 2, lo, hi);
           }
@@ -431,27 +457,62 @@ __global__ void __launch_bounds__(512, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(sb(s, FB_CTX_READY));
-      // ---- out-projection epilogue: r = x + (acc + bo), LN2, y
-      const bool valid = row < S;
-      const float* xr = a.x + (t0 + row) * DM;
-      float4 xn[8];   // residual row, one 32-column chunk ahead of its use
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        xn[c] = valid ? __ldg(reinterpret_cast<const float4*>(xr + 4 * c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      // ---- out-projection epilogue: r = x + (acc + bo), LN2, y.
+      // The residual x arrives by TMA as 128-row x 32-column fp32 chunks (16 KB,
+      // 128-byte swizzle): chunk 0 into the k|v buffer (free since the last
+      // P v), chunks 1-2 into the two halves of ctx once the out-projection has
+      // read it, chunk 3 into k|v again once chunk 0 is consumed.
+      constexpr int NXC = DM / 32;                       // 4 (d=128) or 2 (d=64)
+      const bool leader = (q == 0 && lane == 0);
+      uint8_t* xbuf = slot_k(s);
+      uint8_t* cbuf = slot_c(s);
+      const int x0_uses = (NXC + 2) / 3;                 // chunks 0 and 3 share k|v
+      if (leader) {
+        mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
+        tma_load_3d(xbuf, &map_x, sb(s, FB_X0), 0, 0, seq);
+      }
       if (!mbar_wait(sb(s, FB_OUT_FULL), pi & 1, abort_flag)) break;
       tc_fence_after();
+      if (leader) {
+        for (int cc = 1; cc < NXC && cc < 3; ++cc) {
+          uint64_t* bar = sb(s, cc == 1 ? FB_X1 : FB_X2);
+          mbar_arrive_expect_tx(bar, 16384);
+          tma_load_3d(cbuf + (cc - 1) * 16384, &map_x, bar, cc * 32, 0, seq);
+        }
+      }
       {
-        float sum = 0.f;
+        // Statistics in one pass over the shifted values r - r0 (r0 = the row's
+        // first element): var = E[(r-r0)^2] - E[r-r0]^2 has no cancellation when
+        // the row's spread is small next to its mean.
+        float shift = 0.f, sum = 0.f, sumsq = 0.f;
+        bool xok = true;
 #pragma unroll 1
-        for (int cc = 0; cc < DM / 32; ++cc) {
-          float4 xc[8];
+        for (int cc = 0; cc < NXC; ++cc) {
+          uint64_t* bar;
+          uint32_t par;
+          const uint8_t* src;
+          if (cc == 0 || cc == 3) {
+            bar = sb(s, FB_X0);
+            par = (uint32_t)(pi * x0_uses + (cc == 3 ? 1 : 0)) & 1;
+            src = xbuf;
+          } else {
+            bar = sb(s, cc == 1 ? FB_X1 : FB_X2);
+            par = (uint32_t)pi & 1;
+            src = cbuf + (cc - 1) * 16384;
+          }
+          if (!mbar_wait(bar, par, abort_flag)) { xok = false; break; }
+          float xv[32];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) xc[c] = xn[c];
-          if (cc + 1 < DM / 32) {
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              xn[c] = valid ? __ldg(reinterpret_cast<const float4*>(xr + (cc + 1) * 32 + 4 * c))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int c = 0; c < 8; ++c) {
+            const float4 t4 = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
+            xv[4 * c + 0] = t4.x; xv[4 * c + 1] = t4.y; xv[4 * c + 2] = t4.z; xv[4 * c + 3] = t4.w;
+          }
+          if (cc == 0 && NXC > 3) {   // every row has read chunk 0: k|v takes chunk 3
+            named_bar_sync(1 + s, 128);
+            if (leader) {
+              mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
+              tma_load_3d(xbuf, &map_x, sb(s, FB_X0), 96, 0, seq);
+            }
           }
           uint32_t r[32];
           tmem_ld32(tb + 32 * cc, r);
@@ -459,11 +520,14 @@ __global__ void __launch_bounds__(512, 1)
           for (int c = 0; c < 8; ++c) {
             const int col = cc * 32 + 4 * c;
             const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bo + col));
-            const float a0 = xc[c].x + (__uint_as_float(r[4 * c + 0]) + bb.x);
-            const float a1 = xc[c].y + (__uint_as_float(r[4 * c + 1]) + bb.y);
-            const float a2 = xc[c].z + (__uint_as_float(r[4 * c + 2]) + bb.z);
-            const float a3 = xc[c].w + (__uint_as_float(r[4 * c + 3]) + bb.w);
-            sum += (a0 + a1) + (a2 + a3);
+            const float a0 = xv[4 * c + 0] + (__uint_as_float(r[4 * c + 0]) + bb.x);
+            const float a1 = xv[4 * c + 1] + (__uint_as_float(r[4 * c + 1]) + bb.y);
+            const float a2 = xv[4 * c + 2] + (__uint_as_float(r[4 * c + 2]) + bb.z);
+            const float a3 = xv[4 * c + 3] + (__uint_as_float(r[4 * c + 3]) + bb.w);
+            if (cc == 0 && c == 0) shift = a0;
+            const float d0 = a0 - shift, d1 = a1 - shift, d2 = a2 - shift, d3 = a3 - shift;
+            sum += (d0 + d1) + (d2 + d3);
+            sumsq += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
             r[4 * c + 0] = __float_as_uint(a0);
             r[4 * c + 1] = __float_as_uint(a1);
             r[4 * c + 2] = __float_as_uint(a2);
@@ -471,55 +535,46 @@ __global__ void __launch_bounds__(512, 1)
           }
           tmem_st32(tb + 32 * cc, r);
         }
-        const float mean = sum * inv_d;
-        float sq = 0.f;
+        named_bar_sync(1 + s, 128);   // all x chunks read: their buffers take y
+        if (!xok) break;
+        const float dmean = sum * inv_d;
+        const float mean = shift + dmean;
+        const float rstd = rsqrtf(fmaxf(sumsq * inv_d - dmean * dmean, 0.f) + a.eps2);
+        // y leaves one 32-column fp32 atom (16 KB, 128-byte swizzle) at a time
+        // through free buffers -- the two halves of ctx, then k|v -- by TMA
+        // store (rows >= S are clipped); a buffer is reused only after TMA has
+        // read it.
 #pragma unroll 1
-        for (int cc = 0; cc < DM / 32; ++cc) {
+        for (int cc = 0; cc < NXC; ++cc) {
+          uint8_t* ybuf = (cc == 2) ? xbuf : (cbuf + (cc & 1) * 16384);
+          if (cc == 3) {   // ctx half 0 again: y chunk 0's store must have read it
+            if (leader) bulk_wait_read<2>();
+            named_bar_sync(1 + s, 128);
+          }
           uint32_t r[32];
           tmem_ld32(tb + 32 * cc, r);
+          const uint32_t dst = smem_u32(ybuf) + row * 128;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float dv = __uint_as_float(r[i]) - mean;
-            sq += dv * dv;
-          }
-        }
-        const float rstd = rsqrtf(sq * inv_d + a.eps2);
-        // y leaves through the (now free) ctx buffer: 32-column fp32 atoms in the
-        // 128-byte swizzled layout, stored by TMA (rows >= S are clipped).
-        constexpr int ATOMS_PER_ROUND = C::A_BYTES / 16384;   // 2 for d=128, 1 for d=64
-        constexpr int ROUNDS = (DM / 32) / ATOMS_PER_ROUND;
-        const uint8_t* cbuf = slot_c(s);
-        const bool leader = (q == 0 && lane == 0);
-#pragma unroll 1
-        for (int rd = 0; rd < ROUNDS; ++rd) {
-#pragma unroll 1
-          for (int j = 0; j < ATOMS_PER_ROUND; ++j) {
-            const int cc = rd * ATOMS_PER_ROUND + j;
-            uint32_t r[32];
-            tmem_ld32(tb + 32 * cc, r);
-            const uint32_t dst = c_base + (uint32_t)j * 16384 + row * 128;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              const int col = cc * 32 + 4 * c;
-              const float4 wv = __ldg(reinterpret_cast<const float4*>(a.ln2_w + col));
-              const float4 bb = __ldg(reinterpret_cast<const float4*>(a.ln2_b + col));
-              st_shared_v4(dst + ((c ^ (row & 7)) << 4),
-                           __float_as_uint((__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bb.x),
-                           __float_as_uint((__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bb.y),
-                           __float_as_uint((__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bb.z),
-                           __float_as_uint((__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bb.w));
-            }
+          for (int c = 0; c < 8; ++c) {
+            const int col = cc * 32 + 4 * c;
+            const float4 wv = __ldg(reinterpret_cast<const float4*>(a.ln2_w + col));
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(a.ln2_b + col));
+            st_shared_v4(dst + ((c ^ (row & 7)) << 4),
+                         __float_as_uint((__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bb.x),
+                         __float_as_uint((__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bb.y),
+                         __float_as_uint((__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bb.z),
+                         __float_as_uint((__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bb.w));
           }
           fence_proxy_async_smem();
           named_bar_sync(1 + s, 128);
           if (leader) {
-            for (int j = 0; j < ATOMS_PER_ROUND; ++j)
-              tma_store_3d(&map_y, cbuf + j * 16384, (rd * ATOMS_PER_ROUND + j) * 32, 0, seq);
+            tma_store_3d(&map_y, ybuf, cc * 32, 0, seq);
             bulk_commit();
-            bulk_wait_read_all();   // the buffer may be rewritten once TMA has read it
           }
-          named_bar_sync(1 + s, 128);
         }
+        // ctx and k|v are rewritten by the next sequence: wait until TMA has read them.
+        if (leader) bulk_wait_read_all();
+        named_bar_sync(1 + s, 128);
       }
       tc_fence_before();
       __syncwarp();
