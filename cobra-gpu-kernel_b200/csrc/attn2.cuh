@@ -1,0 +1,314 @@
+// attn2.cuh -- K2 for head_dim <= 64: flash attention with two query tiles
+// per CTA and P kept in tensor memory.
+//
+// Same arithmetic as attn.cuh (BaselineSelfAttention.forward,
+// torch_transformer_benchmark.py:98-113, without materialising the scores);
+// the schedule is built for the long-sequence configs (S up to 100000,
+// head_dim 32 / 64), where the exponentials, not the tensor core, set the pace:
+//   * a work item is (b, h, 256 queries) = two 128-row query tiles that share
+//     every K / v^T tile (one TMA load feeds two S MMAs);
+//   * two softmax warpgroups, one per query tile, so one tile's softmax runs
+//     while the tensor core computes the other tile's S and P v;
+//   * P is written back to TMEM as fp16 pairs and consumed by
+//     tcgen05.mma with A from TMEM, so P never touches shared memory;
+//   * K / v^T stream through a 3-stage TMA ring; lazy rescaling of O (only when
+//     a row max grows by more than 2^8).
+// TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
+// O0 [384, 384+dhp) O1 [384+dhp, 384+2*dhp).
+// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 4-7 softmax of tile 0,
+// 8-11 softmax of tile 1 (one query row per thread).
+#pragma once
+
+#include "attn.cuh"
+#include "common.cuh"
+
+namespace b200l {
+
+template <int DHP>
+struct Attn2Cfg {
+  static constexpr int BN = 128;
+  static constexpr int QKROW = DHP >= 64 ? 128 : 64;   // bytes per swizzled Q/K row
+  static constexpr int QKC = DHP * 2 / QKROW;          // atom columns along dh
+  static constexpr int Q_BYTES = 128 * DHP * 2;        // one query tile
+  static constexpr int K_BYTES = BN * DHP * 2;
+  static constexpr int V_BYTES = DHP * BN * 2;         // v^T tile: DHP rows x 128 keys
+  static constexpr int KVST = 3;
+  static constexpr int SMEM = 2 * Q_BYTES + KVST * (K_BYTES + V_BYTES) + 256 + 1024;
+  static constexpr int S_COL = 0, P_COL = 256, O_COL = 384;
+};
+
+template <int DHP>
+__global__ void __launch_bounds__(384, 1)
+    attn2_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                 const __grid_constant__ CUtensorMap map_vt, AttnArgs args, DevStatus* status) {
+  using C = Attn2Cfg<DHP>;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                  // Q0 | Q1
+  uint8_t* sK = sQ + 2 * C::Q_BYTES;
+  uint8_t* sV = sK + C::KVST * C::K_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + C::KVST * C::V_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;    // [3]
+  uint64_t* kv_empty = bars + 5;   // [3]
+  uint64_t* s_full = bars + 8;     // [2]
+  uint64_t* s_free = bars + 10;    // [2]
+  uint64_t* p_full = bars + 12;    // [2]
+  uint64_t* pv_done = bars + 14;   // [2]
+  uint64_t* mma_done = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = args.S;
+  const int QP = (S + 255) / 256;                       // query pairs per (b, h)
+  const int num_items = args.B * args.H * QP;
+  const int NKV_ALL = (S + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_free[t], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&pv_done[t], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_vt);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // Query tiles an item has (the second one may lie entirely past S) and the
+  // key tiles it visits (causal items stop after their last query).
+  auto item_nqt = [&](int item) -> int { return (S - (item % QP) * 256) > 128 ? 2 : 1; };
+  auto item_nkv = [&](int item) -> int {
+    if (!args.causal) return NKV_ALL;
+    const int qend = min(S, (item % QP) * 256 + 256);
+    return (qend + BN - 1) / BN;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {  // ================= TMA producer
+      int g = 0, it = 0, lastkv[3] = {-1, -1, -1}, lastq = -1;
+      bool ok = true;
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++it) {
+        const int bh = item / QP, q0 = (item % QP) * 256;
+        const int nqt = item_nqt(item);
+        if (!mbar_wait(q_empty, (it & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full, nqt * C::Q_BYTES);
+        for (int t = 0; t < nqt; ++t)
+          for (int kc = 0; kc < C::QKC; ++kc)
+            tma_load_3d(sQ + t * C::Q_BYTES + kc * 128 * C::QKROW, &map_q, q_full, kc * 64, q0 + t * 128, bh);
+        lastq = it;
+        const int nkv = item_nkv(item);
+        for (int j = 0; j < nkv; ++j, ++g) {
+          const int st = g % C::KVST;
+          if (!mbar_wait(&kv_empty[st], ((g / C::KVST) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[st], C::K_BYTES + C::V_BYTES);
+          for (int kc = 0; kc < C::QKC; ++kc)
+            tma_load_3d(sK + st * C::K_BYTES + kc * BN * C::QKROW, &map_k, &kv_full[st], kc * 64, j * BN, bh);
+          for (int kc = 0; kc < BN / 64; ++kc)
+            tma_load_3d(sV + st * C::V_BYTES + kc * DHP * 128, &map_vt, &kv_full[st], j * BN + kc * 64, 0, bh);
+          lastkv[st] = g;
+        }
+      }
+      if (lastq >= 0) mbar_drain(q_full, lastq & 1);
+      for (int i = 0; i < 3; ++i)
+        if (lastkv[i] >= 0) mbar_drain(&kv_full[i], (lastkv[i] / C::KVST) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ================= MMA issuer
+      const uint32_t idesc_s = idesc_f16_f32(128, BN);
+      const uint32_t idesc_o = idesc_f16_f32(128, DHP);
+      int g = 0, it = 0, n[2] = {0, 0};   // n[t]: tiles tile t has processed (barrier phases)
+      bool ok = true;
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++it) {
+        const int nqt = item_nqt(item);
+        const int nkv = item_nkv(item);
+        if (!mbar_wait(q_full, it & 1, abort_flag)) break;
+        for (int j = 0; j <= nkv && ok; ++j) {
+          if (j < nkv) {  // S_t = Q_t K_j^T for both query tiles
+            const int st = (g + j) % C::KVST;
+            if (!mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, abort_flag)) { ok = false; break; }
+            const uint32_t k_base = smem_u32(sK + st * C::K_BYTES);
+            for (int t = 0; t < nqt; ++t) {
+              const int nt = n[t] + j;
+              if (nt > 0 && !mbar_wait(&s_free[t], (nt - 1) & 1, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t q_base = smem_u32(sQ + t * C::Q_BYTES);
+#pragma unroll
+              for (int k = 0; k < DHP / 16; ++k) {
+                const uint32_t off_q = (uint32_t)((k * 32) / C::QKROW) * (128 * C::QKROW) + (k * 32) % C::QKROW;
+                const uint32_t off_k = (uint32_t)((k * 32) / C::QKROW) * (BN * C::QKROW) + (k * 32) % C::QKROW;
+                umma_f16_ss(tmem_base + C::S_COL + t * 128, sdesc_kmajor(q_base + off_q, C::QKROW),
+                            sdesc_kmajor(k_base + off_k, C::QKROW), idesc_s, k > 0 ? 1u : 0u);
+              }
+              umma_commit(&s_full[t]);
+            }
+            if (!ok) break;
+            if (j == nkv - 1) umma_commit(q_empty);
+          }
+          if (j > 0) {  // O_t += P_t V_{j-1}, P_t from TMEM
+            const int gp = g + j - 1;
+            const int st = gp % C::KVST;
+            const uint32_t v_base = smem_u32(sV + st * C::V_BYTES);
+            for (int t = 0; t < nqt; ++t) {
+              const int nt = n[t] + j - 1;
+              if (!mbar_wait(&p_full[t], nt & 1, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+#pragma unroll
+              for (int k = 0; k < BN / 16; ++k)
+                umma_f16_ts(tmem_base + C::O_COL + t * DHP, tmem_base + C::P_COL + t * 64 + k * 8,
+                            sdesc_kmajor(v_base + (uint32_t)(k >> 2) * (DHP * 128) + (k & 3) * 32, 128), idesc_o,
+                            (j > 1 || k > 0) ? 1u : 0u);
+              umma_commit(&pv_done[t]);
+            }
+            if (!ok) break;
+            umma_commit(&kv_empty[st]);
+          }
+        }
+        g += nkv;
+        for (int t = 0; t < nqt; ++t) n[t] += nkv;
+      }
+      umma_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+  } else if (warp >= 4) {  // ================= softmax: tile t, one query row per thread
+    const int t = (warp - 4) >> 2;
+    const int qd = warp & 3;
+    const int row = qd * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+    const uint32_t t_s = tmem_base + lane_off + C::S_COL + t * 128;
+    const uint32_t t_p = tmem_base + lane_off + C::P_COL + t * 64;
+    const uint32_t t_o = tmem_base + lane_off + C::O_COL + t * DHP;
+    const float sl2 = args.scale_log2;
+    int n = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+      if (t >= item_nqt(item)) continue;
+      const int bh = item / QP;
+      const int q0 = (item % QP) * 256 + t * 128;
+      const int qpos = q0 + row;
+      const int nkv = item_nkv(item);
+      float m_use = 0.f, l = 0.f;
+      for (int j = 0; j < nkv; ++j, ++n) {
+        if (!mbar_wait(&s_full[t], n & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        float s[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_s + c * 32, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[t]);
+
+        const int kv0 = j * BN;
+        const bool need_mask = (kv0 + BN > S) || (args.causal && kv0 + BN - 1 > q0);
+        if (need_mask) {
+          const int lim = args.causal ? min(S, qpos + 1) : S;  // keys [0, lim) are visible
+#pragma unroll
+          for (int c = 0; c < BN; ++c)
+            if (kv0 + c >= lim) s[c] = -INFINITY;
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+        const float m_cand = mx * sl2;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (j == 0) {
+          m_use = (m_cand == -INFINITY) ? 0.f : m_cand;
+        } else if (m_cand > m_use + 8.f) {
+          alpha = ex2_approx(m_use - m_cand);
+          m_use = m_cand;
+          rescale = true;
+        }
+        if (j > 0) {
+          // P_t and O_t belong to the previous P v until it completes.
+          if (!mbar_wait(&pv_done[t], (n - 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+            for (int c = 0; c < DHP / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld32(t_o + c * 32, r);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+              tmem_st32(t_o + c * 32, r);
+            }
+          }
+        }
+        // p = 2^(s*scale*log2e - m), packed as fp16 pairs straight into TMEM.
+        float rs = 0.f;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float p0 = ex2_approx(fmaf(s[64 * h2 + 2 * i], sl2, -m_use));
+            const float p1 = ex2_approx(fmaf(s[64 * h2 + 2 * i + 1], sl2, -m_use));
+            rs += p0 + p1;
+            pk[i] = pack_half2(p0, p1);
+          }
+          tmem_st32(t_p + 32 * h2, pk);
+        }
+        l = l * alpha + rs;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (!ok) break;
+      // ---- epilogue: ctx row = O / l (fp16); rows beyond S are not stored.
+      if (!mbar_wait(&pv_done[t], (n - 1) & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const float inv_l = 1.0f / l;
+      const int b = bh / args.H, h = bh % args.H;
+      __half* dst = args.ctx + ((long long)b * S + qpos) * args.d + (long long)h * args.dh;
+#pragma unroll 1
+      for (int c = 0; c < DHP / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_o + c * 32, r);
+        if (qpos < S && c * 32 < args.dh) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            d4[v] = make_uint4(pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l),
+                               pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l),
+                               pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l),
+                               pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l));
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kAttn, 1);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace b200l

@@ -19,6 +19,7 @@
 
 #include "../../include/cobra_b200.h"
 #include "attn.cuh"
+#include "attn2.cuh"
 #include "common.cuh"
 #include "fused_layer.cuh"
 #include "gemm.cuh"
@@ -279,7 +280,9 @@ int run_qkv(const b200l_layer_desc* desc, const Plan& p, const float* x, void* w
   return launch_gemm_tma_t<256, 4, EPI_QKV>(map_a, map_b, ea, p.T, p.d, 3 * p.d, ws, st);
 }
 
-template <int DHP, int BN>
+// TWO_TILE: the two-query-tile kernel with P in TMEM (head_dim <= 64);
+// otherwise one query tile per item with P in shared memory.
+template <int DHP, int BN, bool TWO_TILE = false>
 int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, void* ws, cudaStream_t st) {
   uint8_t* w = static_cast<uint8_t*>(ws);
   const unsigned long long BH = (unsigned long long)p.B * p.H;
@@ -308,19 +311,30 @@ int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& de
   a.causal = desc->causal ? 1 : 0;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)p.dh));
   a.num_items = (int)(BH * (unsigned long long)((p.S + 127) / 128));
-  auto kern = attn_kernel<DHP, BN>;
-  const int smem = AttnCfg<DHP, BN>::SMEM;
-  int rc = ensure_smem((const void*)kern, smem);
-  if (rc) return rc;
-  const int grid = a.num_items < dev.sms ? a.num_items : dev.sms;
-  kern<<<grid, 192, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
-  return check_launch("attn_kernel");
+  if constexpr (TWO_TILE) {
+    auto kern = attn2_kernel<DHP>;
+    const int smem = Attn2Cfg<DHP>::SMEM;
+    int rc = ensure_smem((const void*)kern, smem);
+    if (rc) return rc;
+    const long long items = (long long)BH * ((p.S + 255) / 256);
+    const int grid = items < dev.sms ? (int)items : dev.sms;
+    kern<<<grid, 384, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
+    return check_launch("attn2_kernel");
+  } else {
+    auto kern = attn_kernel<DHP, BN>;
+    const int smem = AttnCfg<DHP, BN>::SMEM;
+    int rc = ensure_smem((const void*)kern, smem);
+    if (rc) return rc;
+    const int grid = a.num_items < dev.sms ? a.num_items : dev.sms;
+    kern<<<grid, 192, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
+    return check_launch("attn_kernel");
+  }
 }
 
 int run_attn(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, void* ws, cudaStream_t st) {
   switch (p.dhp) {
-    case 32: return launch_attn_t<32, 128>(desc, p, dev, ws, st);
-    case 64: return launch_attn_t<64, 128>(desc, p, dev, ws, st);
+    case 32: return launch_attn_t<32, 128, true>(desc, p, dev, ws, st);
+    case 64: return launch_attn_t<64, 128, true>(desc, p, dev, ws, st);
     case 128: return launch_attn_t<128, 128>(desc, p, dev, ws, st);
     default: return launch_attn_t<256, 64>(desc, p, dev, ws, st);
   }
