@@ -231,9 +231,13 @@ __global__ void __launch_bounds__(384, 1)
           for (int c = 0; c < BN; ++c)
             if (kv0 + c >= lim) s[c] = -INFINITY;
         }
-        float mx = s[0];
+        float m8[8];   // eight independent running maxima: short dependency chains
 #pragma unroll
-        for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+        for (int k = 0; k < 8; ++k) m8[k] = s[k];
+#pragma unroll
+        for (int c = 8; c < BN; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
+        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         const float m_cand = mx * sl2;
         float alpha = 1.f;
         bool rescale = false;
@@ -260,20 +264,24 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         // p = 2^(s*scale*log2e - m), packed as fp16 pairs straight into TMEM.
-        float rs = 0.f;
+        float r4[4] = {0.f, 0.f, 0.f, 0.f};   // independent partial sums
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
           uint32_t pk[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float p0 = ex2_approx(fmaf(s[64 * h2 + 2 * i], sl2, -m_use));
-            const float p1 = ex2_approx(fmaf(s[64 * h2 + 2 * i + 1], sl2, -m_use));
-            rs += p0 + p1;
+            // 3 of every 8 pairs on the FMA pipe, the rest on MUFU
+            const float x0 = fmaf(s[64 * h2 + 2 * i], sl2, -m_use);
+            const float x1 = fmaf(s[64 * h2 + 2 * i + 1], sl2, -m_use);
+            const bool poly = (i & 7) < 3;
+            const float p0 = poly ? ex2_poly(x0) : ex2_approx(x0);
+            const float p1 = poly ? ex2_poly(x1) : ex2_approx(x1);
+            r4[i & 3] += p0 + p1;
             pk[i] = pack_half2(p0, p1);
           }
           tmem_st32(t_p + 32 * h2, pk);
         }
-        l = l * alpha + rs;
+        l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);

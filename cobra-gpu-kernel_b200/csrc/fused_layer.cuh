@@ -398,21 +398,26 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_after();
         const int lim = a.causal ? min(S, row + 1) : S;  // keys [0, lim) are visible
         const bool full = (lim == 128);
-        float mx = -INFINITY;
+        float m8[8];   // eight independent running maxima: short dependency chains
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = -INFINITY;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
           tmem_ld32(tb + 128 + 32 * c, r);
           if (full) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+            for (int i = 0; i < 32; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(r[i]));
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, (32 * c + i < lim) ? __uint_as_float(r[i]) : -INFINITY);
+            for (int i = 0; i < 32; ++i)
+              m8[i & 7] = fmaxf(m8[i & 7], (32 * c + i < lim) ? __uint_as_float(r[i]) : -INFINITY);
           }
         }
+        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         const float ms = mx * sl2;
-        float l = 0.f;
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32], pk[16];
@@ -425,11 +430,12 @@ __global__ void __launch_bounds__(512, 1)
             const float s1 = (full || k0 + 1 < lim) ? __uint_as_float(r[2 * i + 1]) : -INFINITY;
             const float p0 = ex2_approx(fmaf(s0, sl2, -ms));
             const float p1 = ex2_approx(fmaf(s1, sl2, -ms));
-            l += p0 + p1;
+            l4[i & 3] += p0 + p1;
             pk[i] = pack_half2(p0, p1);
           }
           tmem_st16(tb + 128 + 16 * c, pk);  // P overwrites the S columns already read
         }
+        const float l = (l4[0] + l4[1]) + (l4[2] + l4[3]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_P_READY));
@@ -508,6 +514,9 @@ __global__ void __launch_bounds__(512, 1)
             xv[4 * c + 0] = t4.x; xv[4 * c + 1] = t4.y; xv[4 * c + 2] = t4.z; xv[4 * c + 3] = t4.w;
           }
           if (cc == 0 && NXC > 3) {   // every row has read chunk 0: k|v takes chunk 3
+            // The TMA write that follows is in the async proxy: order this thread's
+            // generic reads of the buffer before it (a plain bar.sync does not).
+            fence_proxy_async_smem();
             named_bar_sync(1 + s, 128);
             if (leader) {
               mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
@@ -535,6 +544,7 @@ __global__ void __launch_bounds__(512, 1)
           }
           tmem_st32(tb + 32 * cc, r);
         }
+        fence_proxy_async_smem();     // x reads before the TMA stores that reuse the buffers
         named_bar_sync(1 + s, 128);   // all x chunks read: their buffers take y
         if (!xok) break;
         const float dmean = sum * inv_d;
@@ -546,7 +556,8 @@ __global__ void __launch_bounds__(512, 1)
         // read it.
 #pragma unroll 1
         for (int cc = 0; cc < NXC; ++cc) {
-          uint8_t* ybuf = (cc == 2) ? xbuf : (cbuf + (cc & 1) * 16384);
+          // chunk -> staging buffer: 0 ctx half 0, 1 ctx half 1, 2 k|v, 3 ctx half 0 again
+          uint8_t* ybuf = (cc == 2) ? xbuf : (cbuf + (cc == 1 ? 16384 : 0));
           if (cc == 3) {   // ctx half 0 again: y chunk 0's store must have read it
             if (leader) bulk_wait_read<2>();
             named_bar_sync(1 + s, 128);

@@ -276,3 +276,24 @@ def test_fused_layer_matches_three_kernel_path(pkg, cuda_ok, shape):
     _close("fused vs three-kernel", yf, y3, 1e-3, 1e-3)
     res = compare_outputs(y_ref, yf.cpu())
     assert res.passed, f"fused layer gate failed: {res}"
+
+
+def test_fused_cfg2_every_sequence_matches_three_kernel_path(pkg, cuda_ok):
+    """Full-size cfg2 (10000 sequences, ~34 sequence pairs per persistent CTA):
+    every output row of the whole-layer kernel against the three-kernel path,
+    three runs, so a rare ordering bug in the long persistent loop shows."""
+    B, S, d, H = 10000, 128, 128, 4
+    cfg, ref, lay = make_layer(pkg, B, S, d, H, False)
+    x, _ = generate_random_case(cfg, seed=77)
+    xg = x.cuda()
+    with torch.inference_mode():
+        y3 = run_stepwise(pkg, lay, xg).clone()
+        bad_rows = []
+        for _ in range(3):
+            yf = lay(xg).clone()
+            torch.cuda.synchronize()
+            lay.check_status()
+            err = (yf - y3).abs().amax(dim=-1)               # [B, S]
+            bad = torch.nonzero(err > 1e-3)
+            bad_rows.append(bad[:8].tolist())
+            assert bad.shape[0] == 0, f"{bad.shape[0]} rows differ, first {bad_rows[-1]}, max {err.max():.3e}"
