@@ -231,13 +231,13 @@ __global__ void __launch_bounds__(384, 1)
           for (int c = 0; c < BN; ++c)
             if (kv0 + c >= lim) s[c] = -INFINITY;
         }
-        float m8[8];   // eight independent running maxima: short dependency chains
+        // Row max: eight independent chains of three-input maxima.
+        float m8[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = s[k];
+        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(s[2 * k], s[2 * k + 1]);
 #pragma unroll
-        for (int c = 8; c < BN; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
-        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int i = 8; i < BN / 2; ++i) m8[i & 7] = fmax3f(m8[i & 7], s[2 * i], s[2 * i + 1]);
+        const float mx = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         const float m_cand = mx * sl2;
         float alpha = 1.f;
         bool rescale = false;
@@ -264,24 +264,32 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         // p = 2^(s*scale*log2e - m), packed as fp16 pairs straight into TMEM.
-        float r4[4] = {0.f, 0.f, 0.f, 0.f};   // independent partial sums
+        // Pairs go through packed fp32x2 FMA/add; 3 of every 8 pairs take the
+        // FMA-pipe exp2, the rest MUFU.
+        const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_use, -m_use);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t pk[32];
+        for (int qq = 0; qq < 4; ++qq) {   // a quarter row (32 keys -> 16 fp16 pairs) at a time
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            // 3 of every 8 pairs on the FMA pipe, the rest on MUFU
-            const float x0 = fmaf(s[64 * h2 + 2 * i], sl2, -m_use);
-            const float x1 = fmaf(s[64 * h2 + 2 * i + 1], sl2, -m_use);
-            const bool poly = (i & 7) < 3;
-            const float p0 = poly ? ex2_poly(x0) : ex2_approx(x0);
-            const float p1 = poly ? ex2_poly(x1) : ex2_approx(x1);
-            r4[i & 3] += p0 + p1;
-            pk[i] = pack_half2(p0, p1);
+          for (int i = 0; i < 16; ++i) {
+            const int e = 32 * qq + 2 * i;
+            const float2 xx = __ffma2_rn(make_float2(s[e], s[e + 1]), sc2, nm2);
+            float2 pp;
+            if ((i & 7) < 3) {
+              pp = ex2_poly2(xx);
+            } else {
+              pp.x = ex2_approx(xx.x);
+              pp.y = ex2_approx(xx.y);
+            }
+            acc[i & 3] = __fadd2_rn(acc[i & 3], pp);
+            pk[i] = pack_half2(pp.x, pp.y);
           }
-          tmem_st32(t_p + 32 * h2, pk);
+          tmem_st16(t_p + 16 * qq, pk);
         }
-        l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
+        const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
+        l = l * alpha + ((a01.x + a01.y) + (a23.x + a23.y));
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);

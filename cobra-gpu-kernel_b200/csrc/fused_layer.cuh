@@ -407,7 +407,8 @@ __global__ void __launch_bounds__(512, 1)
           tmem_ld32(tb + 128 + 32 * c, r);
           if (full) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(r[i]));
+            for (int i = 0; i < 16; ++i)
+              m8[i & 7] = fmax3f(m8[i & 7], __uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
@@ -417,7 +418,8 @@ __global__ void __launch_bounds__(512, 1)
         const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                                fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         const float ms = mx * sl2;
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+        const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-ms, -ms);
+        float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32], pk[16];
@@ -428,14 +430,15 @@ __global__ void __launch_bounds__(512, 1)
             // masked keys: exp2(-inf) = 0
             const float s0 = (full || k0 < lim) ? __uint_as_float(r[2 * i]) : -INFINITY;
             const float s1 = (full || k0 + 1 < lim) ? __uint_as_float(r[2 * i + 1]) : -INFINITY;
-            const float p0 = ex2_approx(fmaf(s0, sl2, -ms));
-            const float p1 = ex2_approx(fmaf(s1, sl2, -ms));
-            l4[i & 3] += p0 + p1;
-            pk[i] = pack_half2(p0, p1);
+            const float2 xx = __ffma2_rn(make_float2(s0, s1), sc2, nm2);
+            const float2 pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+            acc[i & 1] = __fadd2_rn(acc[i & 1], pp);
+            pk[i] = pack_half2(pp.x, pp.y);
           }
           tmem_st16(tb + 128 + 16 * c, pk);  // P overwrites the S columns already read
         }
-        const float l = (l4[0] + l4[1]) + (l4[2] + l4[3]);
+        const float2 a01 = __fadd2_rn(acc[0], acc[1]);
+        const float l = a01.x + a01.y;
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_P_READY));
