@@ -212,12 +212,11 @@ __global__ void __launch_bounds__(384, 1)
         if (!mbar_wait(&s_full[t], n & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
+        {
+          uint32_t r[BN];   // the whole score row in one TMEM load
+          tmem_ld128(t_s, r);
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_s + c * 32, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+          for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(r[i]);
         }
         tc_fence_before();
         __syncwarp();
