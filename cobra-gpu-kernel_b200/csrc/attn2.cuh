@@ -263,8 +263,7 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         // p = 2^(s*scale*log2e - m), packed as fp16 pairs straight into TMEM.
-        // Pairs go through packed fp32x2 FMA/add; 3 of every 8 pairs take the
-        // FMA-pipe exp2, the rest MUFU.
+        // Pairs go through packed fp32x2 FMA/add, exponentials through MUFU.
         const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_use, -m_use);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
@@ -275,13 +274,7 @@ __global__ void __launch_bounds__(384, 1)
           for (int i = 0; i < 16; ++i) {
             const int e = 32 * qq + 2 * i;
             const float2 xx = __ffma2_rn(make_float2(s[e], s[e + 1]), sc2, nm2);
-            float2 pp;
-            if ((i & 7) < 3) {
-              pp = ex2_poly2(xx);
-            } else {
-              pp.x = ex2_approx(xx.x);
-              pp.y = ex2_approx(xx.y);
-            }
+            const float2 pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
             acc[i & 3] = __fadd2_rn(acc[i & 3], pp);
             pk[i] = pack_half2(pp.x, pp.y);
           }
