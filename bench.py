@@ -230,6 +230,8 @@ def main() -> int:
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard-chunks", type=int, default=2,
+                    help="pieces per rank for the scatter/gather measurement (N > 1)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (smaller cases for ncu captures)")
     args = ap.parse_args()
@@ -352,6 +354,36 @@ def main() -> int:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
 
+        # ---- N > 1: the config's own batch held on rank 0's device, split by
+        # ShardedLayer (x slices sent, y slices gathered back over NCCL
+        # send/recv). Strong scaling; reported beside the weak-scaling value.
+        sharded = None
+        if world > 1:
+            del xd, xh, yh
+            sl = pkg.ShardedLayer(layer, src=0, chunks=args.shard_chunks)
+            xg = x if rank == 0 else None
+            for _ in range(2):
+                sl(xg)
+            torch.cuda.synchronize(dev)
+            sh_steps = max(3, min(args.steps, 10))
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(sh_steps):
+                sl(xg)
+            s1.record(stream)
+            torch.cuda.synchronize(dev)
+            layer.check_status()
+            t = torch.tensor([s0.elapsed_time(s1) / sh_steps], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sh_ms = float(t.item())
+            sharded = {"value": T / (sh_ms / 1e3), "unit": "tokens/s", "ms_per_step": sh_ms,
+                       "global_batch": B, "per_gpu_batch": -(-B // world), "chunks": args.shard_chunks,
+                       "scaling": "strong", "steps": sh_steps,
+                       "path": "ShardedLayer.forward: x on rank 0's device, slices over NCCL "
+                               "send/recv, y gathered into rank 0's output"}
+
     ms_per_step = total_ms / args.steps
     value = world * T / (ms_per_step / 1e3)
     pk_ = peaks()
@@ -404,6 +436,8 @@ def main() -> int:
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+    if sharded is not None:
+        line["sharded_from_rank0"] = sharded
     print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

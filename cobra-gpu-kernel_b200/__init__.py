@@ -2,10 +2,13 @@
 
 Public API (mirrors dalberrt/COBRA-GPU-Kernel's drop-in module):
     TransformerConfig, B200TransformerLayer, SelfAttentionWeights
+    ShardedLayer / sharded_forward: the layer split by batch over one process per GPU
 Native boundary: ``include/cobra_b200.h`` (ctypes binding in ``_lib``).
 """
 
 from .layer import B200TransformerLayer, SelfAttentionWeights, TransformerConfig  # noqa: F401
 from . import _lib  # noqa: F401
+from .sharding import ShardedLayer, batch_shards, sharded_forward  # noqa: F401
 
-__all__ = ["B200TransformerLayer", "SelfAttentionWeights", "TransformerConfig"]
+__all__ = ["B200TransformerLayer", "SelfAttentionWeights", "TransformerConfig",
+           "ShardedLayer", "batch_shards", "sharded_forward"]

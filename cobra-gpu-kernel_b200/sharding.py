@@ -1,0 +1,193 @@
+"""Batch-sharded layer forward, one process per GPU over ``torch.distributed``.
+
+Every op of the layer works on one sequence at a time
+(torch_transformer_benchmark.py:1446-1447, ``tools/sweep.py:62-65``), so the
+batch splits into contiguous slices of ceil(B / n) sequences, one per rank,
+with no reduction collective. The caller's rank (``src``) holds x; it sends
+each rank its slice, runs its own slice, and receives the other ranks' y
+slices straight into its output tensor. Transfers are point-to-point
+(NCCL send/recv over NVLink/NVSwitch with the ``nccl`` backend; the same code
+runs on ``gloo`` for CPU tests) and are split into ``chunks`` pieces per
+rank so that a rank computes piece i while piece i+1 is still arriving.
+
+Weights are replicated: every rank builds or loads the same layer. With
+B < n only the first B ranks receive work; the rest still take part in the
+header broadcast and return at once. Head sharding (for B < n) is not
+offered: the out-projection mixes heads, so it would need an all-gather of
+ctx before the residual and LayerNorm.
+
+Failure behaviour: the caller's input is validated on ``src`` before any data
+moves and the verdict is broadcast, so a bad input raises the same
+``ValueError`` on every rank. A rank that fails after the header (a kernel
+error, an exception in ``layer``) leaves its peers waiting on a transfer that
+never comes; the process group's timeout ends their wait with an error.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+__all__ = ["batch_shards", "sharded_forward", "ShardedLayer"]
+
+# Header broadcast from src: status, B, S, d, has_mask.
+_HDR_OK = 0
+_HDR_BAD_RANK = 1
+_HDR_BAD_SHAPE = 2
+_HDR_BAD_DTYPE = 3
+_HDR_BAD_MASK = 4
+_HDR_MESSAGES = {
+    _HDR_BAD_RANK: "src rank passed no input tensor",
+    _HDR_BAD_SHAPE: "x must be a [B, S, d] tensor with B, S, d > 0",
+    _HDR_BAD_DTYPE: "x must be float32",
+    _HDR_BAD_MASK: "valid_token_mask must be a [B, S] bool tensor",
+}
+
+
+def batch_shards(batch: int, world: int) -> List[Tuple[int, int]]:
+    """Half-open sequence ranges [start, stop) for ranks 0..world-1.
+
+    Contiguous slices of ceil(batch / world) sequences; ranks past the last
+    slice get an empty range (start == stop == batch)."""
+    if batch < 0 or world <= 0:
+        raise ValueError(f"bad batch/world: {batch}, {world}")
+    per = -(-batch // world) if batch else 0
+    out = []
+    for r in range(world):
+        a = min(batch, r * per)
+        b = min(batch, a + per)
+        out.append((a, b))
+    return out
+
+
+def _chunk_ranges(a: int, b: int, chunks: int) -> List[Tuple[int, int]]:
+    n = b - a
+    if n <= 0:
+        return []
+    k = max(1, min(chunks, n))
+    per = -(-n // k)
+    return [(a + i, min(b, a + i + per)) for i in range(0, n, per)]
+
+
+def _default_device(backend: str) -> torch.device:
+    if backend == "nccl":
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cpu")
+
+
+def _validate(x: Optional[torch.Tensor], mask: Optional[torch.Tensor]) -> int:
+    if x is None:
+        return _HDR_BAD_RANK
+    if x.dim() != 3 or min(x.shape) <= 0:
+        return _HDR_BAD_SHAPE
+    if x.dtype != torch.float32:
+        return _HDR_BAD_DTYPE
+    if mask is not None and (mask.dtype != torch.bool or tuple(mask.shape) != tuple(x.shape[:2])):
+        return _HDR_BAD_MASK
+    return _HDR_OK
+
+
+def sharded_forward(layer: Callable[..., torch.Tensor], x: Optional[torch.Tensor] = None,
+                    valid_token_mask: Optional[torch.Tensor] = None, *, src: int = 0,
+                    group: Optional[dist.ProcessGroup] = None, device: Optional[torch.device] = None,
+                    chunks: int = 1) -> Optional[torch.Tensor]:
+    """Run ``layer`` over the batch of ``x`` split across the ranks of ``group``.
+
+    Collective: every rank of ``group`` calls it; ``x`` (fp32 [B, S, d] on this
+    rank's device) and the optional ``valid_token_mask`` ([B, S] bool) are
+    read on ``src`` only. ``layer(x_slice, mask_slice)`` must map [b, S, d] to
+    [b, S, d] sequence by sequence (``B200TransformerLayer`` does). Returns y
+    [B, S, d] on ``src`` (the slices computed by the ranks, gathered into one
+    tensor) and ``None`` on every other rank.
+    """
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    src_g = dist.get_global_rank(group, src) if group is not None else src
+    backend = dist.get_backend(group)
+    if rank == src:
+        device = x.device if x is not None else (device or _default_device(backend))
+    elif device is None:
+        device = _default_device(backend)
+
+    hdr = torch.zeros(5, dtype=torch.int64, device=device)
+    if rank == src:
+        status = _validate(x, valid_token_mask)
+        hdr[0] = status
+        if status == _HDR_OK:
+            hdr[1:4] = torch.tensor(x.shape, dtype=torch.int64)
+            hdr[4] = 1 if valid_token_mask is not None else 0
+    dist.broadcast(hdr, src_g, group=group)
+    status, B, S, d, has_mask = (int(v) for v in hdr.tolist())
+    if status != _HDR_OK:
+        raise ValueError(f"sharded_forward: {_HDR_MESSAGES[status]} (validated on rank {src})")
+
+    shards = batch_shards(B, world)
+    works = []
+    if rank == src:
+        x = x.contiguous()
+        mask = valid_token_mask.to(torch.uint8).contiguous() if has_mask else None
+        y = torch.empty_like(x)
+        # Post every transfer first: x slices out, y slices back into y.
+        for r, (a, b) in enumerate(shards):
+            if r == src or a == b:
+                continue
+            peer = dist.get_global_rank(group, r) if group is not None else r
+            for c0, c1 in _chunk_ranges(a, b, chunks):
+                works.append(dist.isend(x[c0:c1], peer, group=group))
+                if mask is not None:
+                    works.append(dist.isend(mask[c0:c1], peer, group=group))
+            for c0, c1 in _chunk_ranges(a, b, chunks):
+                works.append(dist.irecv(y[c0:c1], peer, group=group))
+        a, b = shards[src]
+        for c0, c1 in _chunk_ranges(a, b, chunks):
+            m = mask[c0:c1].bool() if mask is not None else None
+            y[c0:c1].copy_(layer(x[c0:c1], m))
+        for w in works:
+            w.wait()
+        return y
+
+    a, b = shards[rank]
+    if a == b:
+        return None
+    xs = torch.empty(b - a, S, d, dtype=torch.float32, device=device)
+    ms = torch.empty(b - a, S, dtype=torch.uint8, device=device) if has_mask else None
+    ys = torch.empty_like(xs)
+    pieces = []
+    for c0, c1 in _chunk_ranges(a, b, chunks):
+        wx = dist.irecv(xs[c0 - a:c1 - a], src_g, group=group)
+        wm = dist.irecv(ms[c0 - a:c1 - a], src_g, group=group) if ms is not None else None
+        pieces.append((c0 - a, c1 - a, wx, wm))
+    for c0, c1, wx, wm in pieces:
+        wx.wait()
+        if wm is not None:
+            wm.wait()
+        m = ms[c0:c1].bool() if ms is not None else None
+        # Copy out of the layer's result: it may be a static buffer that the
+        # next call overwrites while the send is still reading it.
+        ys[c0:c1].copy_(layer(xs[c0:c1], m))
+        works.append(dist.isend(ys[c0:c1], src_g, group=group))
+    for w in works:
+        w.wait()
+    return None
+
+
+class ShardedLayer(torch.nn.Module):
+    """``forward(x, valid_token_mask=None)`` of a replicated layer, sharded by batch.
+
+    Wraps a layer (every rank holds the same weights) so that the caller's
+    rank sees the reference module's API; see ``sharded_forward``."""
+
+    def __init__(self, layer: torch.nn.Module, *, src: int = 0,
+                 group: Optional[dist.ProcessGroup] = None, chunks: int = 1) -> None:
+        super().__init__()
+        self.layer = layer
+        self.src = src
+        self.group = group
+        self.chunks = chunks
+
+    def forward(self, x: Optional[torch.Tensor] = None,
+                valid_token_mask: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+        return sharded_forward(self.layer, x, valid_token_mask, src=self.src, group=self.group,
+                               chunks=self.chunks)

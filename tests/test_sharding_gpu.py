@@ -1,0 +1,78 @@
+"""Batch sharding over NCCL on two B200s: the gathered output is bitwise equal
+to the one-GPU output (every sequence runs the same kernels either way).
+
+Skipped unless two sm_100 devices are visible. Ranks are spawned processes,
+one per GPU, with a short process-group timeout.
+"""
+
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parent.parent
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # (B, S, d, H, causal, chunks): whole-layer kernel, three-kernel path, causal, B < world
+    (37, 128, 128, 4, False, 1),
+    (37, 128, 128, 4, False, 3),
+    (6, 300, 256, 4, False, 2),
+    (5, 200, 128, 2, True, 1),
+    (1, 64, 128, 4, False, 1),
+]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, root: str) -> None:
+    import datetime
+    sys.path.insert(0, root)
+    import torch.distributed as dist
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from oracle import TransformerConfig, build_reference_layer, generate_random_case
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        with torch.inference_mode():
+            for B, S, d, H, causal, chunks in CASES:
+                cfg = TransformerConfig(B, S, d, H, causal=causal)
+                ref = build_reference_layer(cfg, seed=21)
+                layer = pkg.B200TransformerLayer(d, H, causal).to(dev).eval()
+                layer.load_state_dict(ref.state_dict(), strict=True)
+                x, _ = generate_random_case(cfg, seed=22)
+                x = x.to(dev)
+                y = pkg.sharded_forward(layer, x if rank == 0 else None, chunks=chunks)
+                torch.cuda.synchronize(dev)
+                layer.check_status()
+                if rank == 0:
+                    single = layer(x).clone()
+                    torch.cuda.synchronize(dev)
+                    assert torch.equal(y, single), f"case {(B, S, d, H, causal, chunks)}"
+                else:
+                    assert y is None
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_forward_two_gpus_bitwise(pkg):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    if any(torch.cuda.get_device_capability(i)[0] != 10 for i in range(2)):
+        pytest.skip("needs sm_100 devices")
+    mp.start_processes(_worker, args=(2, _free_port(), str(ROOT)), nprocs=2, join=True,
+                       start_method="spawn")
