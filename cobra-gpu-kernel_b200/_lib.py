@@ -20,7 +20,7 @@ EXPORTED = (
     "b200l_outproj_res_ln", "b200l_layer_forward_noalloc",
 )
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Size of the library's built-in scratch used by b200l_layer_forward_noalloc.
 NOALLOC_MAX_SCRATCH_BYTES = 64 * 1024 * 1024
@@ -45,6 +45,7 @@ class LayerDesc(ctypes.Structure):
         ("num_heads", c_int32), ("causal", c_int32), ("eps1", c_float), ("eps2", c_float),
         ("wqkv", c_void_p), ("bqkv", c_void_p), ("wo", c_void_p), ("bo", c_void_p),
         ("ln1_w", c_void_p), ("ln1_b", c_void_p), ("ln2_w", c_void_p), ("ln2_b", c_void_p),
+        ("valid_mask", c_void_p),
     ]
 
 

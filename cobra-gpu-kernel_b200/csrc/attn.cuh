@@ -31,6 +31,7 @@ struct AttnArgs {
   int causal;
   float scale_log2;  // dh^-0.5 * log2(e)
   int num_items;     // B*H*ceil(S/128)
+  const uint8_t* kmask;  // key-padding mask uint8 [B, S] (nonzero = valid), or nullptr
 };
 
 template <int DHP, int BN>
@@ -49,7 +50,7 @@ struct AttnCfg {
   static constexpr int TMEM_COLS = (BN + DHP) <= 256 ? 256 : 512;
 };
 
-template <int DHP, int BN>
+template <int DHP, int BN, bool KMASK>   // KMASK: a key-padding mask may be given
 __global__ void __launch_bounds__(192, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_vt, AttnArgs args, DevStatus* status) {
@@ -214,7 +215,10 @@ __global__ void __launch_bounds__(192, 1)
       const int qpos = q0 + row;
       const int nkv = item_nkv(item);
       float m_use = 0.f, l = 0.f;
+      const uint8_t* mrow = (KMASK && args.kmask) ? args.kmask + (long long)(bh / args.H) * S : nullptr;
       for (int j = 0; j < nkv; ++j, ++g) {
+        uint32_t kb[BN / 32];
+        if (KMASK && mrow) key_mask_load<BN / 32>(mrow, j * BN, S, lane, kb);
         if (!mbar_wait(s_full, g & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
@@ -236,6 +240,17 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int c = 0; c < BN; ++c)
             if (kv0 + c >= lim) s[c] = -INFINITY;
+        }
+        if (KMASK && mrow) {   // key padding: invalid keys get probability 0 (-inf score)
+          key_mask_ballot<BN / 32>(kb);
+          uint32_t all = kb[0];
+#pragma unroll
+          for (int w = 1; w < BN / 32; ++w) all &= kb[w];
+          if (all != 0xffffffffu) {
+#pragma unroll
+            for (int c = 0; c < BN; ++c)
+              if (!((kb[c >> 5] >> (c & 31)) & 1u)) s[c] = -INFINITY;
+          }
         }
         float mx = s[0];
 #pragma unroll
@@ -288,7 +303,7 @@ __global__ void __launch_bounds__(192, 1)
       // ---- epilogue: ctx row = O / l (fp16), rows beyond S are not stored.
       if (!mbar_wait(pv_done, (g - 1) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const float inv_l = 1.0f / l;
+      const float inv_l = l > 0.f ? 1.0f / l : 0.f;   // a row with every key masked -> 0
       const int b = bh / args.H, h = bh % args.H;
       __half* dst = args.ctx + ((long long)b * S + qpos) * args.d + (long long)h * args.dh;
 #pragma unroll 1

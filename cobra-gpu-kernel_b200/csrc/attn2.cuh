@@ -9,12 +9,17 @@
 //     every K / v^T tile (one TMA load feeds two S MMAs);
 //   * two softmax warpgroups, one per query tile, so one tile's softmax runs
 //     while the tensor core computes the other tile's S and P v;
-//   * P is written back to TMEM as fp16 pairs and consumed by
-//     tcgen05.mma with A from TMEM, so P never touches shared memory;
+//   * S lands in one of three 128-column TMEM buffers used round-robin by the
+//     two tiles; the softmax writes P (fp16 pairs) over the S it has read, and
+//     tcgen05.mma reads P from TMEM as its A operand, so P never touches shared
+//     memory. A buffer is reused for the S three allocations later, which the
+//     MMA issuer enqueues only after the P v that reads the buffer, so the
+//     exponentials never wait for a P v to finish (only an O rescale does);
 //   * K / v^T stream through a 3-stage TMA ring; lazy rescaling of O (only when
 //     a row max grows by more than 2^8).
-// TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
+// TMEM (512 columns): S/P buffers [0,128) [128,256) [256,384),
 // O0 [384, 384+dhp) O1 [384+dhp, 384+2*dhp).
+// MMA order per key tile j: S_0(j), P_0 v(j-1), S_1(j), P_1 v(j-1).
 // Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 4-7 softmax of tile 0,
 // 8-11 softmax of tile 1 (one query row per thread).
 #pragma once
@@ -34,10 +39,11 @@ struct Attn2Cfg {
   static constexpr int V_BYTES = DHP * BN * 2;         // v^T tile: DHP rows x 128 keys
   static constexpr int KVST = 3;
   static constexpr int SMEM = 2 * Q_BYTES + KVST * (K_BYTES + V_BYTES) + 256 + 1024;
-  static constexpr int S_COL = 0, P_COL = 256, O_COL = 384;
+  static constexpr int NSB = 3;                        // S/P buffers of 128 columns
+  static constexpr int O_COL = 384;
 };
 
-template <int DHP>
+template <int DHP, bool KMASK>   // KMASK: a key-padding mask may be given
 __global__ void __launch_bounds__(384, 1)
     attn2_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                  const __grid_constant__ CUtensorMap map_vt, AttnArgs args, DevStatus* status) {
@@ -53,9 +59,8 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* q_empty = bars + 1;
   uint64_t* kv_full = bars + 2;    // [3]
   uint64_t* kv_empty = bars + 5;   // [3]
-  uint64_t* s_full = bars + 8;     // [2]
-  uint64_t* s_free = bars + 10;    // [2]
-  uint64_t* p_full = bars + 12;    // [2]
+  uint64_t* s_full = bars + 8;     // [3] one per S/P buffer
+  uint64_t* p_full = bars + 12;    // [2] one per query tile
   uint64_t* pv_done = bars + 14;   // [2]
   uint64_t* mma_done = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
@@ -74,9 +79,8 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
+    for (int b = 0; b < C::NSB; ++b) mbar_init(&s_full[b], 1);
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], 4);
       mbar_init(&p_full[t], 4);
       mbar_init(&pv_done[t], 1);
     }
@@ -137,55 +141,53 @@ __global__ void __launch_bounds__(384, 1)
     if (lane == 0) {  // ================= MMA issuer
       const uint32_t idesc_s = idesc_f16_f32(128, BN);
       const uint32_t idesc_o = idesc_f16_f32(128, DHP);
-      int g = 0, it = 0, n[2] = {0, 0};   // n[t]: tiles tile t has processed (barrier phases)
+      // a: S allocations so far (buffer a % 3); g: key tiles so far (ring stage);
+      // np[t]: P v steps of tile t so far (p_full / pv_done phases).
+      int a = 0, g = 0, it = 0, np[2] = {0, 0};
       bool ok = true;
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++it) {
         const int nqt = item_nqt(item);
         const int nkv = item_nkv(item);
         if (!mbar_wait(q_full, it & 1, abort_flag)) break;
         for (int j = 0; j <= nkv && ok; ++j) {
-          if (j < nkv) {  // S_t = Q_t K_j^T for both query tiles
-            const int st = (g + j) % C::KVST;
-            if (!mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, abort_flag)) { ok = false; break; }
-            const uint32_t k_base = smem_u32(sK + st * C::K_BYTES);
-            for (int t = 0; t < nqt; ++t) {
-              const int nt = n[t] + j;
-              if (nt > 0 && !mbar_wait(&s_free[t], (nt - 1) & 1, abort_flag)) { ok = false; break; }
-              tc_fence_after();
+          const int st = (g + j) % C::KVST;
+          if (j < nkv && !mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, abort_flag)) { ok = false; break; }
+          for (int t = 0; t < nqt; ++t) {
+            if (j < nkv) {  // S_t(j) = Q_t K_j^T into buffer a % 3. Its previous
+              // user, allocation a - 3, had its P v enqueued before this MMA.
+              const int n = a + j * nqt + t;
+              const uint32_t k_base = smem_u32(sK + st * C::K_BYTES);
               const uint32_t q_base = smem_u32(sQ + t * C::Q_BYTES);
+              tc_fence_after();
 #pragma unroll
               for (int k = 0; k < DHP / 16; ++k) {
                 const uint32_t off_q = (uint32_t)((k * 32) / C::QKROW) * (128 * C::QKROW) + (k * 32) % C::QKROW;
                 const uint32_t off_k = (uint32_t)((k * 32) / C::QKROW) * (BN * C::QKROW) + (k * 32) % C::QKROW;
-                umma_f16_ss(tmem_base + C::S_COL + t * 128, sdesc_kmajor(q_base + off_q, C::QKROW),
+                umma_f16_ss(tmem_base + (uint32_t)(n % C::NSB) * 128, sdesc_kmajor(q_base + off_q, C::QKROW),
                             sdesc_kmajor(k_base + off_k, C::QKROW), idesc_s, k > 0 ? 1u : 0u);
               }
-              umma_commit(&s_full[t]);
+              umma_commit(&s_full[n % C::NSB]);
+              if (j == nkv - 1 && t == nqt - 1) umma_commit(q_empty);
             }
-            if (!ok) break;
-            if (j == nkv - 1) umma_commit(q_empty);
-          }
-          if (j > 0) {  // O_t += P_t V_{j-1}, P_t from TMEM
-            const int gp = g + j - 1;
-            const int st = gp % C::KVST;
-            const uint32_t v_base = smem_u32(sV + st * C::V_BYTES);
-            for (int t = 0; t < nqt; ++t) {
-              const int nt = n[t] + j - 1;
-              if (!mbar_wait(&p_full[t], nt & 1, abort_flag)) { ok = false; break; }
+            if (j > 0) {  // O_t += P_t(j-1) v_{j-1}, P from its S/P buffer in TMEM
+              const int n = a + (j - 1) * nqt + t;
+              const int stp = (g + j - 1) % C::KVST;
+              const uint32_t v_base = smem_u32(sV + stp * C::V_BYTES);
+              if (!mbar_wait(&p_full[t], np[t] & 1, abort_flag)) { ok = false; break; }
               tc_fence_after();
 #pragma unroll
               for (int k = 0; k < BN / 16; ++k)
-                umma_f16_ts(tmem_base + C::O_COL + t * DHP, tmem_base + C::P_COL + t * 64 + k * 8,
+                umma_f16_ts(tmem_base + C::O_COL + t * DHP, tmem_base + (uint32_t)(n % C::NSB) * 128 + k * 8,
                             sdesc_kmajor(v_base + (uint32_t)(k >> 2) * (DHP * 128) + (k & 3) * 32, 128), idesc_o,
                             (j > 1 || k > 0) ? 1u : 0u);
               umma_commit(&pv_done[t]);
+              ++np[t];
+              if (t == nqt - 1) umma_commit(&kv_empty[stp]);
             }
-            if (!ok) break;
-            umma_commit(&kv_empty[st]);
           }
         }
+        a += nqt * nkv;
         g += nkv;
-        for (int t = 0; t < nqt; ++t) n[t] += nkv;
       }
       umma_commit(mma_done);
       mbar_drain(mma_done, 0);
@@ -195,21 +197,28 @@ __global__ void __launch_bounds__(384, 1)
     const int qd = warp & 3;
     const int row = qd * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    const uint32_t t_s = tmem_base + lane_off + C::S_COL + t * 128;
-    const uint32_t t_p = tmem_base + lane_off + C::P_COL + t * 64;
     const uint32_t t_o = tmem_base + lane_off + C::O_COL + t * DHP;
     const float sl2 = args.scale_log2;
-    int n = 0;
+    int a = 0, np = 0;   // S allocations before this item; P v steps of tile t so far
     bool ok = true;
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-      if (t >= item_nqt(item)) continue;
+      const int nqt = item_nqt(item);
+      const int nkv = item_nkv(item);
+      if (t >= nqt) {
+        a += nqt * nkv;
+        continue;
+      }
       const int bh = item / QP;
       const int q0 = (item % QP) * 256 + t * 128;
       const int qpos = q0 + row;
-      const int nkv = item_nkv(item);
       float m_use = 0.f, l = 0.f;
-      for (int j = 0; j < nkv; ++j, ++n) {
-        if (!mbar_wait(&s_full[t], n & 1, abort_flag)) { ok = false; break; }
+      const uint8_t* mrow = (KMASK && args.kmask) ? args.kmask + (long long)(bh / args.H) * S : nullptr;
+      for (int j = 0; j < nkv; ++j, ++np) {
+        const int n = a + j * nqt + t;
+        const uint32_t t_s = tmem_base + lane_off + (uint32_t)(n % C::NSB) * 128;
+        uint32_t kb[BN / 32];
+        if (KMASK && mrow) key_mask_load<BN / 32>(mrow, j * BN, S, lane, kb);
+        if (!mbar_wait(&s_full[n % C::NSB], (n / C::NSB) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
         {
@@ -218,9 +227,6 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(r[i]);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[t]);
 
         const int kv0 = j * BN;
         const bool need_mask = (kv0 + BN > S) || (args.causal && kv0 + BN - 1 > q0);
@@ -229,6 +235,17 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int c = 0; c < BN; ++c)
             if (kv0 + c >= lim) s[c] = -INFINITY;
+        }
+        if (KMASK && mrow) {   // key padding: invalid keys get probability 0 (-inf score)
+          key_mask_ballot<BN / 32>(kb);
+          uint32_t all = kb[0];
+#pragma unroll
+          for (int w = 1; w < BN / 32; ++w) all &= kb[w];
+          if (all != 0xffffffffu) {
+#pragma unroll
+            for (int c = 0; c < BN; ++c)
+              if (!((kb[c >> 5] >> (c & 31)) & 1u)) s[c] = -INFINITY;
+          }
         }
         // Row max: eight independent chains of three-input maxima.
         float m8[8];
@@ -247,22 +264,7 @@ __global__ void __launch_bounds__(384, 1)
           m_use = m_cand;
           rescale = true;
         }
-        if (j > 0) {
-          // P_t and O_t belong to the previous P v until it completes.
-          if (!mbar_wait(&pv_done[t], (n - 1) & 1, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-            for (int c = 0; c < DHP / 32; ++c) {
-              uint32_t r[32];
-              tmem_ld32(t_o + c * 32, r);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-              tmem_st32(t_o + c * 32, r);
-            }
-          }
-        }
-        // p = 2^(s*scale*log2e - m), packed as fp16 pairs straight into TMEM.
+        // p = 2^(s*scale*log2e - m), packed as fp16 pairs over the S just read.
         // Pairs go through packed fp32x2 FMA/add, exponentials through MUFU.
         const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_use, -m_use);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
@@ -278,19 +280,34 @@ __global__ void __launch_bounds__(384, 1)
             acc[i & 3] = __fadd2_rn(acc[i & 3], pp);
             pk[i] = pack_half2(pp.x, pp.y);
           }
-          tmem_st16(t_p + 16 * qq, pk);
+          tmem_st16_async(t_s + 16 * qq, pk);
         }
         const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
         l = l * alpha + ((a01.x + a01.y) + (a23.x + a23.y));
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+          // O_t is the previous P v's accumulator until that MMA completes.
+          if (!mbar_wait(&pv_done[t], (np - 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < DHP / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(t_o + c * 32, r);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(t_o + c * 32, r);
+          }
+        }
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
+      a += nqt * nkv;
       // ---- epilogue: ctx row = O / l (fp16); rows beyond S are not stored.
-      if (!mbar_wait(&pv_done[t], (n - 1) & 1, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&pv_done[t], (np - 1) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const float inv_l = 1.0f / l;
+      const float inv_l = l > 0.f ? 1.0f / l : 0.f;   // a row with every key masked -> 0
       const int b = bh / args.H, h = bh % args.H;
       __half* dst = args.ctx + ((long long)b * S + qpos) * args.d + (long long)h * args.dh;
 #pragma unroll 1

@@ -311,8 +311,9 @@ int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& de
   a.causal = desc->causal ? 1 : 0;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)p.dh));
   a.num_items = (int)(BH * (unsigned long long)((p.S + 127) / 128));
+  a.kmask = desc->valid_mask;
   if constexpr (TWO_TILE) {
-    auto kern = attn2_kernel<DHP>;
+    auto kern = a.kmask ? attn2_kernel<DHP, true> : attn2_kernel<DHP, false>;
     const int smem = Attn2Cfg<DHP>::SMEM;
     int rc = ensure_smem((const void*)kern, smem);
     if (rc) return rc;
@@ -321,7 +322,7 @@ int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& de
     kern<<<grid, 384, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
     return check_launch("attn2_kernel");
   } else {
-    auto kern = attn_kernel<DHP, BN>;
+    auto kern = a.kmask ? attn_kernel<DHP, BN, true> : attn_kernel<DHP, BN, false>;
     const int smem = AttnCfg<DHP, BN>::SMEM;
     int rc = ensure_smem((const void*)kern, smem);
     if (rc) return rc;
@@ -351,6 +352,7 @@ int run_outproj(const b200l_layer_desc* desc, const Plan& p, const float* x, flo
   ea.ln_b = desc->ln2_b;
   ea.eps = desc->eps2;
   ea.d = p.d;
+  ea.rowmask = desc->valid_mask;
   CUtensorMap map_a, map_b;
   int rc = map_rows_k(&map_a, ctx, (unsigned long long)p.T, p.d, 128, "ctx");
   if (rc) return rc;
@@ -400,7 +402,8 @@ int launch_fused_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& d
   a.ln2_w = desc->ln2_w; a.ln2_b = desc->ln2_b; a.eps2 = desc->eps2;
   a.B = p.B; a.S = p.S; a.causal = desc->causal ? 1 : 0;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt(32.0));
-  auto kern = fused_layer_kernel<DM>;
+  a.mask = desc->valid_mask;
+  auto kern = a.mask ? fused_layer_kernel<DM, true> : fused_layer_kernel<DM, false>;
   const int smem = FusedCfg<DM>::SMEM;
   if ((rc = ensure_smem((const void*)kern, smem))) return rc;
   const int npairs = (p.B + 1) / 2;

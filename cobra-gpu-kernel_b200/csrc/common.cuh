@@ -290,6 +290,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// Store without waiting: several stores can be in flight; tmem_wait_st()
+// waits for all of this thread's earlier TMEM stores.
+__device__ __forceinline__ void tmem_st16_async(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -379,6 +391,26 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// Key-padding mask, one bit per key. A warp reads the mask bytes of keys
+// [kv0, kv0 + 32*NW) of one sequence (``mrow`` = its [S] uint8 row, nonzero =
+// valid) and turns them into NW ballot words: bit i of word w is key
+// kv0 + 32*w + i. Keys at or past S read as valid (the sequence-end mask
+// covers them). Loads and ballots are split so the loads can be issued
+// before a pipeline wait and consumed after it.
+template <int NW>
+__device__ __forceinline__ void key_mask_load(const uint8_t* mrow, int kv0, int S, int lane, uint32_t (&v)[NW]) {
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    const int k = kv0 + 32 * w + lane;
+    v[w] = (k < S) ? (uint32_t)__ldg(mrow + k) : 1u;
+  }
+}
+template <int NW>
+__device__ __forceinline__ void key_mask_ballot(uint32_t (&v)[NW]) {
+#pragma unroll
+  for (int w = 0; w < NW; ++w) v[w] = __ballot_sync(0xffffffffu, v[w] != 0u);
 }
 
 }  // namespace b200l

@@ -47,6 +47,7 @@ struct FusedArgs {
   int B, S;
   int causal;
   float scale_log2;
+  const uint8_t* mask;  // key-padding mask uint8 [B, S] (nonzero = valid), or nullptr
 };
 
 template <int DM>
@@ -68,7 +69,7 @@ struct FusedCfg {
 enum FusedBar : int { FB_A_READY = 0, FB_A_FREE, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY,
                       FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_X0, FB_X1, FB_X2, FB_COUNT };
 
-template <int DM>
+template <int DM, bool KMASK>   // KMASK: a key-padding mask may be given
 __global__ void __launch_bounds__(512, 1)
     fused_layer_kernel(const __grid_constant__ CUtensorMap map_wqkv, const __grid_constant__ CUtensorMap map_wo,
                        const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_y,
@@ -340,6 +341,27 @@ __global__ void __launch_bounds__(512, 1)
       const int seq = 2 * pair + s;
       if (seq >= a.B) break;
       const long long t0 = (long long)seq * S;
+      // Keys this row may see, one bit each: valid (mask), inside S, causal.
+      // A padded query row (mask byte 0) keeps y = LN2(x): its attention
+      // output, bias included, is zeroed (BaselineSelfAttention :106-109, :121-122).
+      const int lim = a.causal ? min(S, row + 1) : S;  // keys [0, lim) are in range
+      uint32_t vb[4] = {0u, 0u, 0u, 0u};
+      bool qkeep = true;
+      if constexpr (KMASK) {
+        uint32_t kb[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+        if (a.mask != nullptr) {
+          key_mask_load<4>(a.mask + t0, 0, S, lane, kb);
+          key_mask_ballot<4>(kb);
+          const uint32_t mine = q == 0 ? kb[0] : q == 1 ? kb[1] : q == 2 ? kb[2] : kb[3];
+          qkeep = ((mine >> lane) & 1u) != 0u;
+        }
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int nb = lim - 32 * w;
+          vb[w] = kb[w] & (nb >= 32 ? 0xffffffffu : (nb <= 0 ? 0u : ((1u << nb) - 1u)));
+        }
+      }
+      const bool full = KMASK ? (vb[0] & vb[1] & vb[2] & vb[3]) == 0xffffffffu : (lim == 128);
       bool ok = true;
       for (int h = 0; h < H; ++h) {
         const int n = pi * H + h;
@@ -396,8 +418,6 @@ __global__ void __launch_bounds__(512, 1)
         // ---- softmax of S = q k^T (one row per thread, exact: S <= 128 keys)
         if (!mbar_wait(sb(s, FB_S_FULL), n & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const int lim = a.causal ? min(S, row + 1) : S;  // keys [0, lim) are visible
-        const bool full = (lim == 128);
         float m8[8];   // eight independent running maxima: short dependency chains
 #pragma unroll
         for (int k = 0; k < 8; ++k) m8[k] = -INFINITY;
@@ -405,6 +425,7 @@ __global__ void __launch_bounds__(512, 1)
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
           tmem_ld32(tb + 128 + 32 * c, r);
+          const uint32_t vw = !KMASK ? 0u : c == 0 ? vb[0] : c == 1 ? vb[1] : c == 2 ? vb[2] : vb[3];
           if (full) {
 #pragma unroll
             for (int i = 0; i < 16; ++i)
@@ -412,24 +433,28 @@ __global__ void __launch_bounds__(512, 1)
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              m8[i & 7] = fmaxf(m8[i & 7], (32 * c + i < lim) ? __uint_as_float(r[i]) : -INFINITY);
+              m8[i & 7] = fmaxf(m8[i & 7], (KMASK ? ((vw >> i) & 1u) != 0u : 32 * c + i < lim)
+                                                 ? __uint_as_float(r[i]) : -INFINITY);
           }
         }
         const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                                fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-        const float ms = mx * sl2;
+        const float ms = (mx == -INFINITY) ? 0.f : mx * sl2;   // every key masked: p = 0, l = 0
         const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-ms, -ms);
         float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32], pk[16];
           tmem_ld32(tb + 128 + 32 * c, r);
+          const uint32_t vw = !KMASK ? 0u : c == 0 ? vb[0] : c == 1 ? vb[1] : c == 2 ? vb[2] : vb[3];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int k0 = 32 * c + 2 * i;
             // masked keys: exp2(-inf) = 0
-            const float s0 = (full || k0 < lim) ? __uint_as_float(r[2 * i]) : -INFINITY;
-            const float s1 = (full || k0 + 1 < lim) ? __uint_as_float(r[2 * i + 1]) : -INFINITY;
+            const int k0 = 32 * c + 2 * i;
+            const bool v0 = KMASK ? ((vw >> (2 * i)) & 1u) != 0u : k0 < lim;
+            const bool v1 = KMASK ? ((vw >> (2 * i + 1)) & 1u) != 0u : k0 + 1 < lim;
+            const float s0 = (full || v0) ? __uint_as_float(r[2 * i]) : -INFINITY;
+            const float s1 = (full || v1) ? __uint_as_float(r[2 * i + 1]) : -INFINITY;
             const float2 xx = __ffma2_rn(make_float2(s0, s1), sc2, nm2);
             const float2 pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
             acc[i & 1] = __fadd2_rn(acc[i & 1], pp);
@@ -448,7 +473,7 @@ __global__ void __launch_bounds__(512, 1)
         {
           uint32_t r[32];
           tmem_ld32(tb + 96, r);
-          const float il = 1.0f / l;
+          const float il = l > 0.f ? 1.0f / l : 0.f;
           const int col0 = 32 * h;
           const uint32_t cb = c_base + (uint32_t)(col0 >> 6) * 16384 + row * 128;
           const int ch0 = (col0 & 63) >> 3;
@@ -532,10 +557,10 @@ __global__ void __launch_bounds__(512, 1)
           for (int c = 0; c < 8; ++c) {
             const int col = cc * 32 + 4 * c;
             const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bo + col));
-            const float a0 = xv[4 * c + 0] + (__uint_as_float(r[4 * c + 0]) + bb.x);
-            const float a1 = xv[4 * c + 1] + (__uint_as_float(r[4 * c + 1]) + bb.y);
-            const float a2 = xv[4 * c + 2] + (__uint_as_float(r[4 * c + 2]) + bb.z);
-            const float a3 = xv[4 * c + 3] + (__uint_as_float(r[4 * c + 3]) + bb.w);
+            const float a0 = xv[4 * c + 0] + (qkeep ? __uint_as_float(r[4 * c + 0]) + bb.x : 0.f);
+            const float a1 = xv[4 * c + 1] + (qkeep ? __uint_as_float(r[4 * c + 1]) + bb.y : 0.f);
+            const float a2 = xv[4 * c + 2] + (qkeep ? __uint_as_float(r[4 * c + 2]) + bb.z : 0.f);
+            const float a3 = xv[4 * c + 3] + (qkeep ? __uint_as_float(r[4 * c + 3]) + bb.w : 0.f);
             if (cc == 0 && c == 0) shift = a0;
             const float d0 = a0 - shift, d1 = a1 - shift, d2 = a2 - shift, d3 = a3 - shift;
             sum += (d0 + d1) + (d2 + d3);

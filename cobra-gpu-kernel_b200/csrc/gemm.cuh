@@ -279,6 +279,7 @@ struct EpiArgs {
   const float* ln_b;
   float eps;
   int d;
+  const uint8_t* rowmask;  // EPI_RESID*: token validity uint8 [T] or nullptr; invalid rows get y = x (+ LN)
 };
 
 template <int BN, int ST>
@@ -390,15 +391,18 @@ __global__ void __launch_bounds__(192, 1)
           if (valid) {
             const float* xr = ea.x + t * ea.d + col0;
             float* yr = ea.y + t * ea.d + col0;
+            // A padded query row's attention output is zeroed (bias included):
+            // y = x there (BaselineSelfAttention, :121-122).
+            const bool keep = ea.rowmask == nullptr || ea.rowmask[t] != 0;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               const float4 xv = __ldg(reinterpret_cast<const float4*>(xr) + c);
               const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.bias + col0) + c);
               float4 o;
-              o.x = xv.x + (__uint_as_float(r[4 * c + 0]) + bv.x);
-              o.y = xv.y + (__uint_as_float(r[4 * c + 1]) + bv.y);
-              o.z = xv.z + (__uint_as_float(r[4 * c + 2]) + bv.z);
-              o.w = xv.w + (__uint_as_float(r[4 * c + 3]) + bv.w);
+              o.x = xv.x + (keep ? __uint_as_float(r[4 * c + 0]) + bv.x : 0.f);
+              o.y = xv.y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
+              o.z = xv.z + (keep ? __uint_as_float(r[4 * c + 2]) + bv.z : 0.f);
+              o.w = xv.w + (keep ? __uint_as_float(r[4 * c + 3]) + bv.w : 0.f);
               reinterpret_cast<float4*>(yr)[c] = o;
             }
           }
@@ -406,6 +410,7 @@ __global__ void __launch_bounds__(192, 1)
       } else {  // EPI_RESID_LN: the whole row is in this tile (n0 == 0, BN >= d)
         const int d = ea.d;
         const float* xr = ea.x + t * d;
+        const bool keep = ea.rowmask == nullptr || (valid && ea.rowmask[t] != 0);  // see EPI_RESID
         float sum = 0.f;
         // pass 1: r = x + (acc + b), written back into TMEM; row sum.
 #pragma unroll 1
@@ -418,10 +423,10 @@ __global__ void __launch_bounds__(192, 1)
             if (valid && col < d) {
               const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + col));
               const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.bias + col));
-              const float a0 = xv.x + (__uint_as_float(r[4 * c + 0]) + bv.x);
-              const float a1 = xv.y + (__uint_as_float(r[4 * c + 1]) + bv.y);
-              const float a2 = xv.z + (__uint_as_float(r[4 * c + 2]) + bv.z);
-              const float a3 = xv.w + (__uint_as_float(r[4 * c + 3]) + bv.w);
+              const float a0 = xv.x + (keep ? __uint_as_float(r[4 * c + 0]) + bv.x : 0.f);
+              const float a1 = xv.y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
+              const float a2 = xv.z + (keep ? __uint_as_float(r[4 * c + 2]) + bv.z : 0.f);
+              const float a3 = xv.w + (keep ? __uint_as_float(r[4 * c + 3]) + bv.w : 0.f);
               sum += (a0 + a1) + (a2 + a3);
               r[4 * c + 0] = __float_as_uint(a0);
               r[4 * c + 1] = __float_as_uint(a1);

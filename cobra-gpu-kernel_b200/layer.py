@@ -28,6 +28,7 @@ import torch.nn as nn
 from . import _lib
 
 GRAPH_MAX_INPUT_BYTES = 64 * 1024 * 1024   # reference gate, torch_transformer_benchmark.py:1077-1079
+HOST_CHUNK_BYTES = 16 * 1024 * 1024        # x bytes per chunk when streaming a host-resident batch
 
 
 @dataclass(frozen=True)
@@ -94,9 +95,12 @@ class B200TransformerLayer(nn.Module):
     """LN1 -> MHA -> +x -> LN2 on B200, with the reference's API.
 
     ``forward(x, valid_token_mask=None)``: x is fp32 [B, S, d] on an sm_100
-    device. The returned tensor may be an internal static buffer that the
-    next call overwrites (as the reference's graph path returns,
-    :1356-1360): copy it if it must outlive the next call.
+    device; ``valid_token_mask`` is an optional [B, S] bool key-padding mask
+    on the same device (True = valid): invalid keys get probability 0 and an
+    invalid query row's attention output is zeroed, so its y is LN2(x)
+    (BaselineSelfAttention :106-109, :121-122). The returned tensor may be an
+    internal static buffer that the next call overwrites (as the reference's
+    graph path returns, :1356-1360): copy it if it must outlive the next call.
     """
 
     def __init__(self, d_model: int, num_heads: int, causal: bool = False, *,
@@ -115,6 +119,9 @@ class B200TransformerLayer(nn.Module):
         self._graph = None
         self._static_x = None
         self._static_y = None
+        self._static_m = None
+        self._host_out = None
+        self._io_streams = None
         self.register_load_state_dict_post_hook(lambda mod, _keys: mod.invalidate())
 
     @classmethod
@@ -128,7 +135,7 @@ class B200TransformerLayer(nn.Module):
         """Drop packed weights and captured graphs (weights changed)."""
         self._pack = None
         self._graph = None
-        self._static_x = self._static_y = None
+        self._static_x = self._static_y = self._static_m = None
         self._sig = None
 
     def _param_versions(self):
@@ -167,7 +174,7 @@ class B200TransformerLayer(nn.Module):
         self._pack = pk
         return pk
 
-    def _desc(self, B: int, S: int, pk: _Pack) -> _lib.LayerDesc:
+    def _desc(self, B: int, S: int, pk: _Pack, mask: Optional[torch.Tensor] = None) -> _lib.LayerDesc:
         att = self.attention
         ln1w, ln1b, bo, ln2w, ln2b = pk.ln
         return _lib.LayerDesc(
@@ -175,7 +182,8 @@ class B200TransformerLayer(nn.Module):
             causal=1 if self.causal else 0, eps1=float(self.norm1.eps), eps2=float(self.norm2.eps),
             wqkv=pk.wqkv16.data_ptr(), bqkv=pk.bqkv32.data_ptr(), wo=pk.wo16.data_ptr(),
             bo=bo.data_ptr(), ln1_w=ln1w.data_ptr(), ln1_b=ln1b.data_ptr(),
-            ln2_w=ln2w.data_ptr(), ln2_b=ln2b.data_ptr())
+            ln2_w=ln2w.data_ptr(), ln2_b=ln2b.data_ptr(),
+            valid_mask=mask.data_ptr() if mask is not None else None)
 
     def _ensure_workspace(self, desc: _lib.LayerDesc, device: torch.device) -> None:
         L = _lib.lib()
@@ -215,44 +223,127 @@ class B200TransformerLayer(nn.Module):
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         if x.dim() != 3 or x.shape[-1] != self.attention.d_model:
             raise ValueError(f"expected x of shape [B, S, {self.attention.d_model}], got {tuple(x.shape)}")
-        if not x.is_cuda:
-            raise RuntimeError("B200TransformerLayer runs only on CUDA (sm_100a) devices; there is no CPU path")
         if x.dtype != torch.float32:
             raise TypeError(f"B200TransformerLayer computes fp32-in/fp32-out; got {x.dtype}")
-        if valid_token_mask is not None and not bool(valid_token_mask.all()):
-            raise NotImplementedError("key-padding masks with padded positions are not supported yet")
+        if not x.is_cuda:
+            if self.norm1.weight.is_cuda:
+                # Host-resident input, parameters on the GPU: stream it through
+                # the device (the reference's _run_streamed, :1418-1508).
+                return self._forward_host(x, valid_token_mask)
+            raise RuntimeError("B200TransformerLayer runs only on CUDA (sm_100a) devices; there is no CPU path")
         B, S, _ = x.shape
+        mask = None
+        if valid_token_mask is not None:
+            # [B, S], True = valid token. Used as its raw bytes (0 / nonzero),
+            # as the reference's fused path does (:1205-1207); no host sync.
+            if tuple(valid_token_mask.shape) != (B, S):
+                raise ValueError(f"valid_token_mask must have shape {(B, S)}, got {tuple(valid_token_mask.shape)}")
+            if valid_token_mask.device != x.device:
+                raise ValueError("valid_token_mask must be on the same device as x")
+            mask = valid_token_mask.to(torch.bool).contiguous().view(torch.uint8)
         x = x.contiguous()
         with torch.cuda.device(x.device):
             pk = self._ensure_pack(x.device)
-            desc = self._desc(B, S, pk)
+            desc = self._desc(B, S, pk, mask)
             self._ensure_workspace(desc, x.device)
-            sig = (B, S, x.device)
+            sig = (B, S, x.device, mask is not None)
             if sig != self._sig:
                 self._sig = sig
                 self._graph = None
-                self._static_x = self._static_y = None
+                self._static_x = self._static_y = self._static_m = None
             small = x.numel() * x.element_size() <= GRAPH_MAX_INPUT_BYTES
             if self.use_graphs and small:
-                return self._run_graphed(x, desc)
+                return self._run_graphed(x, mask, pk)
             y = torch.empty_like(x)
             self._launch(x, y, desc)
             return y
 
-    def _run_graphed(self, x: torch.Tensor, desc: _lib.LayerDesc) -> torch.Tensor:
-        """Capture K1->K2->K3 once per shape, then copy x in and replay."""
+    def _forward_host(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
+        """Host x -> host y through the GPU that holds the parameters.
+
+        Sequences are independent (:1446-1447), so the batch moves in chunks
+        of about HOST_CHUNK_BYTES through a three-stream pipeline: host-to-
+        device copies on one stream, the layer on the caller's current stream,
+        device-to-host copies on a third, with two device buffers for each of
+        x and y. Both PCIe directions and the kernels overlap, so the call
+        costs about one direction's transfer time. Pinned host memory makes
+        the copies asynchronous; the result is a pinned host buffer owned by
+        the module (overwritten by the next host call), complete on return.
+        """
+        dev = self.norm1.weight.device
+        B, S, d = x.shape
+        mask = None
+        if valid_token_mask is not None:
+            if tuple(valid_token_mask.shape) != (B, S):
+                raise ValueError(f"valid_token_mask must have shape {(B, S)}, got {tuple(valid_token_mask.shape)}")
+            mask = valid_token_mask.to(torch.bool).contiguous().view(torch.uint8)
+        x = x.contiguous()
+        cb = max(1, min(B, HOST_CHUNK_BYTES // max(1, S * d * 4)))
+        with torch.cuda.device(dev):
+            pk = self._ensure_pack(dev)
+            self._ensure_workspace(self._desc(cb, S, pk), dev)
+            if self._host_out is None or self._host_out.shape != x.shape:
+                self._host_out = None
+                self._host_out = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
+            out = self._host_out
+            if self._io_streams is None or self._io_streams[0].device != dev:
+                self._io_streams = (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev))
+            h2d, d2h = self._io_streams
+            comp = torch.cuda.current_stream(dev)
+            nbuf = 2 if B > cb else 1
+            xb = [torch.empty(cb, S, d, dtype=torch.float32, device=dev) for _ in range(nbuf)]
+            yb = [torch.empty(cb, S, d, dtype=torch.float32, device=dev) for _ in range(nbuf)]
+            mb = [torch.empty(cb, S, dtype=torch.uint8, device=dev) for _ in range(nbuf)] if mask is not None else None
+            ev_in = [torch.cuda.Event() for _ in range(nbuf)]
+            ev_comp = [torch.cuda.Event() for _ in range(nbuf)]
+            ev_out = [torch.cuda.Event() for _ in range(nbuf)]
+            h2d.wait_stream(comp)      # device buffers were just allocated on comp
+            for i, b0 in enumerate(range(0, B, cb)):
+                b1 = min(B, b0 + cb)
+                n, k = b1 - b0, i % nbuf
+                with torch.cuda.stream(h2d):
+                    if i >= nbuf:
+                        h2d.wait_event(ev_comp[k])        # the layer is done reading xb[k]
+                    xb[k][:n].copy_(x[b0:b1], non_blocking=True)
+                    if mb is not None:
+                        mb[k][:n].copy_(mask[b0:b1], non_blocking=True)
+                    ev_in[k].record(h2d)
+                comp.wait_event(ev_in[k])
+                if i >= nbuf:
+                    comp.wait_event(ev_out[k])            # yb[k] has been copied out
+                self._launch(xb[k][:n], yb[k][:n], self._desc(n, S, pk, mb[k][:n] if mb is not None else None))
+                ev_comp[k].record(comp)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev_comp[k])
+                    out[b0:b1].copy_(yb[k][:n], non_blocking=True)
+                    ev_out[k].record(d2h)
+            comp.wait_stream(d2h)
+            comp.wait_stream(h2d)
+            comp.synchronize()         # y is complete on the host; the buffers are idle
+        return out
+
+    def _run_graphed(self, x: torch.Tensor, mask: Optional[torch.Tensor], pk: _Pack) -> torch.Tensor:
+        """Capture the layer once per shape (and mask / no mask), then copy x
+        (and the mask) into the static buffers and replay."""
         if self._graph is None:
             self._static_x = x.clone()
             self._static_y = torch.empty_like(x)
+            self._static_m = mask.clone() if mask is not None else None
+            B, S, _ = x.shape
+            desc = self._desc(B, S, pk, self._static_m)
             side = torch.cuda.Stream(device=x.device)
             side.wait_stream(torch.cuda.current_stream(x.device))
             with torch.cuda.stream(side):
                 self._launch(self._static_x, self._static_y, desc)   # sets kernel attributes
             torch.cuda.current_stream(x.device).wait_stream(side)
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            # thread_local: other threads (e.g. a NCCL watchdog) may keep
+            # making CUDA calls while this thread captures.
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self._launch(self._static_x, self._static_y, desc)
             self._graph = g
         self._static_x.copy_(x)
+        if mask is not None:
+            self._static_m.copy_(mask)
         self._graph.replay()
         return self._static_y

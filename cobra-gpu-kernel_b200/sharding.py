@@ -123,6 +123,22 @@ def sharded_forward(layer: Callable[..., torch.Tensor], x: Optional[torch.Tensor
     if status != _HDR_OK:
         raise ValueError(f"sharded_forward: {_HDR_MESSAGES[status]} (validated on rank {src})")
 
+    # Run the layer eagerly while transfers are in flight: a CUDA-graph
+    # capture (B200TransformerLayer captures on the first call per shape, and
+    # ragged chunks change the shape) must not overlap NCCL work.
+    saved_graphs = getattr(layer, "use_graphs", None)
+    if saved_graphs:
+        layer.use_graphs = False
+    try:
+        return _exchange(layer, x, valid_token_mask, rank, world, src, src_g, group, device,
+                         B, S, d, has_mask, chunks)
+    finally:
+        if saved_graphs:
+            layer.use_graphs = saved_graphs
+
+
+def _exchange(layer, x, valid_token_mask, rank, world, src, src_g, group, device, B, S, d, has_mask,
+              chunks):
     shards = batch_shards(B, world)
     works = []
     if rank == src:

@@ -48,7 +48,7 @@
 extern "C" {
 #endif
 
-#define B200L_ABI_VERSION 1
+#define B200L_ABI_VERSION 2
 
 enum b200l_status {
     B200L_OK = 0,
@@ -81,6 +81,14 @@ typedef struct b200l_layer_desc {
     const float* ln1_b;
     const float* ln2_w;
     const float* ln2_b;
+    /* Optional key-padding mask, uint8 [B, S] (a torch bool tensor's bytes;
+     * nonzero = valid token), or NULL for none. As in BaselineSelfAttention
+     * (torch_transformer_benchmark.py:106-109, :121-122) and the fused path's
+     * attn_bias / row mask (:1201-1214): invalid keys get probability 0 in
+     * every query's softmax, and an invalid query row's attention output
+     * (after the out-projection and its bias) is zeroed, so that row of y is
+     * LN2(x). Read by the attention and out-projection kernels. */
+    const uint8_t* valid_mask;
 } b200l_layer_desc;
 
 /* ABI version (B200L_ABI_VERSION). */

@@ -30,3 +30,20 @@ def cuda_ok():
     if major != 10:
         pytest.skip("needs an sm_100 device")
     return True
+
+
+def spawn_ranks(fn, args, nprocs, seconds):
+    """Run fn(rank, *args) in nprocs spawned processes; fail (and kill those
+    processes, by PID) if they have not all finished within ``seconds``."""
+    import time
+    import torch.multiprocessing as mp
+    ctx = mp.start_processes(fn, args=args, nprocs=nprocs, join=False, start_method="spawn")
+    deadline = time.monotonic() + seconds
+    while not ctx.join(timeout=2):
+        if time.monotonic() > deadline:
+            for p in ctx.processes:
+                if p.is_alive():
+                    p.kill()
+            for p in ctx.processes:
+                p.join(10)
+            pytest.fail(f"ranks did not finish within {seconds} s")

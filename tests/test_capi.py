@@ -73,3 +73,27 @@ def test_no_cpu_fallback(pkg):
     layer = pkg.B200TransformerLayer(128, 4)
     with pytest.raises(RuntimeError, match="no CPU path"):
         layer(torch.zeros(1, 4, 128))
+
+
+def test_descriptor_layout_matches_header(pkg, tmp_path):
+    """The ctypes mirror of b200l_layer_desc has the C struct's size and field
+    offsets (compiled from include/cobra_b200.h with the host C compiler)."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    D = pkg._lib.LayerDesc
+    names = [f[0] for f in D._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "cobra_b200.h"\nint main(void) {\n'
+        '  printf("%zu\\n", sizeof(b200l_layer_desc));\n'
+        + "".join(f'  printf("%zu\\n", offsetof(b200l_layer_desc, {n}));\n' for n in names)
+        + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(ROOT / "include"), "-o", str(exe), str(src)], check=True)
+    out = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True,
+                                          text=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(D)
+    assert out[1:] == [getattr(D, n).offset for n in names]

@@ -151,8 +151,6 @@ def test_kernels_stepwise(pkg, cuda_ok, shape):
 def test_golden_fixtures(pkg, cuda_ok, path):
     """The reference's own outputs (tests/golden, produced by make_golden.py)."""
     g = torch.load(GOLDEN / path)
-    if g["padding"] > 0:
-        pytest.skip("key-padding masks are not supported by the kernels yet")
     cfg = TransformerConfig(g["B"], g["S"], g["d"], g["H"], causal=g["causal"])
     ref = build_reference_layer(cfg, g["weight_seed"])
     if "state_dict" in g:
@@ -160,8 +158,9 @@ def test_golden_fixtures(pkg, cuda_ok, path):
     lay = pkg.B200TransformerLayer(g["d"], g["H"], g["causal"]).cuda().eval()
     lay.load_state_dict(ref.state_dict(), strict=True)
     for t in g["trials"]:
+        mask = t["mask"].cuda() if g["padding"] > 0 else None
         with torch.inference_mode():
-            y = lay(t["x"].cuda()).clone()
+            y = lay(t["x"].cuda(), mask).clone()
         torch.cuda.synchronize()
         lay.check_status()
         res = compare_outputs(t["y"], y.cpu())

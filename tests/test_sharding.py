@@ -13,7 +13,8 @@ from pathlib import Path
 
 import pytest
 import torch
-import torch.multiprocessing as mp
+
+from tests.conftest import spawn_ranks
 
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -135,8 +136,7 @@ def _worker(rank: int, world: int, port: int, root: str) -> None:
 def test_sharded_forward_gloo_world2(pkg, monkeypatch):
     port = _free_port()
     monkeypatch.setenv("GLOO_SOCKET_IFNAME", "lo")
-    mp.start_processes(_worker, args=(2, port, str(ROOT)), nprocs=2, join=True,
-                       start_method="spawn")
+    spawn_ranks(_worker, (2, port, str(ROOT)), 2, 120)
 
 
 def _failing_worker(rank: int, world: int, port: int, root: str) -> None:
@@ -172,5 +172,4 @@ def _failing_worker(rank: int, world: int, port: int, root: str) -> None:
 def test_sharded_forward_peer_failure_times_out(pkg, monkeypatch):
     port = _free_port()
     monkeypatch.setenv("GLOO_SOCKET_IFNAME", "lo")
-    mp.start_processes(_failing_worker, args=(2, port, str(ROOT)), nprocs=2, join=True,
-                       start_method="spawn")
+    spawn_ranks(_failing_worker, (2, port, str(ROOT)), 2, 120)

@@ -11,7 +11,8 @@ from pathlib import Path
 
 import pytest
 import torch
-import torch.multiprocessing as mp
+
+from tests.conftest import spawn_ranks
 
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -74,5 +75,4 @@ def test_sharded_forward_two_gpus_bitwise(pkg):
         pytest.skip("needs two GPUs")
     if any(torch.cuda.get_device_capability(i)[0] != 10 for i in range(2)):
         pytest.skip("needs sm_100 devices")
-    mp.start_processes(_worker, args=(2, _free_port(), str(ROOT)), nprocs=2, join=True,
-                       start_method="spawn")
+    spawn_ranks(_worker, (2, _free_port(), str(ROOT)), 2, 240)
