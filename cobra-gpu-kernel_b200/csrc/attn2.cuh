@@ -141,6 +141,12 @@ __global__ void __launch_bounds__(384, 1)
     if (lane == 0) {  // ================= MMA issuer
       const uint32_t idesc_s = idesc_f16_f32(128, BN);
       const uint32_t idesc_o = idesc_f16_f32(128, DHP);
+      // Shared-memory descriptors of the first Q / K / v^T tiles; every other
+      // operand is a fixed byte offset away, added to the start-address field
+      // (addresses stay below 256 KB, so the 14-bit field never carries).
+      const uint64_t dq0 = sdesc_kmajor(smem_u32(sQ), C::QKROW);
+      const uint64_t dk0 = sdesc_kmajor(smem_u32(sK), C::QKROW);
+      const uint64_t dv0 = sdesc_kmajor(smem_u32(sV), 128);
       // a: S allocations so far (buffer a % 3); g: key tiles so far (ring stage);
       // np[t]: P v steps of tile t so far (p_full / pv_done phases).
       int a = 0, g = 0, it = 0, np[2] = {0, 0};
@@ -156,15 +162,16 @@ __global__ void __launch_bounds__(384, 1)
             if (j < nkv) {  // S_t(j) = Q_t K_j^T into buffer a % 3. Its previous
               // user, allocation a - 3, had its P v enqueued before this MMA.
               const int n = a + j * nqt + t;
-              const uint32_t k_base = smem_u32(sK + st * C::K_BYTES);
-              const uint32_t q_base = smem_u32(sQ + t * C::Q_BYTES);
+              const uint64_t dq = dq0 + (uint64_t)((t * C::Q_BYTES) >> 4);
+              const uint64_t dk = dk0 + (uint64_t)((st * C::K_BYTES) >> 4);
+              const uint32_t d_s = tmem_base + (uint32_t)(n % C::NSB) * 128;
               tc_fence_after();
 #pragma unroll
               for (int k = 0; k < DHP / 16; ++k) {
-                const uint32_t off_q = (uint32_t)((k * 32) / C::QKROW) * (128 * C::QKROW) + (k * 32) % C::QKROW;
-                const uint32_t off_k = (uint32_t)((k * 32) / C::QKROW) * (BN * C::QKROW) + (k * 32) % C::QKROW;
-                umma_f16_ss(tmem_base + (uint32_t)(n % C::NSB) * 128, sdesc_kmajor(q_base + off_q, C::QKROW),
-                            sdesc_kmajor(k_base + off_k, C::QKROW), idesc_s, k > 0 ? 1u : 0u);
+                constexpr int R = C::QKROW;
+                const uint32_t off_q = (uint32_t)((k * 32) / R) * (128 * R) + (k * 32) % R;
+                const uint32_t off_k = (uint32_t)((k * 32) / R) * (BN * R) + (k * 32) % R;
+                umma_f16_ss(d_s, dq + (off_q >> 4), dk + (off_k >> 4), idesc_s, k > 0 ? 1u : 0u);
               }
               umma_commit(&s_full[n % C::NSB]);
               if (j == nkv - 1 && t == nqt - 1) umma_commit(q_empty);
@@ -172,14 +179,16 @@ __global__ void __launch_bounds__(384, 1)
             if (j > 0) {  // O_t += P_t(j-1) v_{j-1}, P from its S/P buffer in TMEM
               const int n = a + (j - 1) * nqt + t;
               const int stp = (g + j - 1) % C::KVST;
-              const uint32_t v_base = smem_u32(sV + stp * C::V_BYTES);
+              const uint64_t dv = dv0 + (uint64_t)((stp * C::V_BYTES) >> 4);
+              const uint32_t d_o = tmem_base + C::O_COL + t * DHP;
+              const uint32_t a_p = tmem_base + (uint32_t)(n % C::NSB) * 128;
+              const uint32_t acc0 = j > 1 ? 1u : 0u;
               if (!mbar_wait(&p_full[t], np[t] & 1, abort_flag)) { ok = false; break; }
               tc_fence_after();
 #pragma unroll
               for (int k = 0; k < BN / 16; ++k)
-                umma_f16_ts(tmem_base + C::O_COL + t * DHP, tmem_base + (uint32_t)(n % C::NSB) * 128 + k * 8,
-                            sdesc_kmajor(v_base + (uint32_t)(k >> 2) * (DHP * 128) + (k & 3) * 32, 128), idesc_o,
-                            (j > 1 || k > 0) ? 1u : 0u);
+                umma_f16_ts(d_o, a_p + k * 8, dv + ((uint32_t)((k >> 2) * (DHP * 128) + (k & 3) * 32) >> 4), idesc_o,
+                            k > 0 ? 1u : acc0);
               umma_commit(&pv_done[t]);
               ++np[t];
               if (t == nqt - 1) umma_commit(&kv_empty[stp]);
