@@ -391,6 +391,15 @@ __device__ __forceinline__ uint32_t swz_offset(int row, int chunk, int row_bytes
 __device__ __forceinline__ void st_shared_u16(uint32_t addr, unsigned short v) {
   asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
 }
+// Streaming 16-byte global load: read-only, not kept in L1 (data used once
+// must not evict the small parameter vectors every thread re-reads).
+__device__ __forceinline__ float4 ldg_stream_f4(const void* p) {
+  float4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }

@@ -61,7 +61,9 @@ struct FusedCfg {
   static constexpr int K_BYTES = 128 * 64;           // 128 keys x 32 fp16, 64-byte swizzle
   static constexpr int V_BYTES = 2 * 32 * 128;       // v^T: 32 x 128 keys, two 64-key atom columns
   static constexpr int SLOT = 2 * A_BYTES + K_BYTES + V_BYTES;
-  static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + 1024;
+  static constexpr int PARAM_BYTES = 3 * DM * 4;     // bo, ln2_w, ln2_b in shared memory
+  static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + PARAM_BYTES + 1024;
+  static_assert(SMEM <= 232448, "fits the 227 KB opt-in shared memory of one CTA");
   static_assert(4 + 2 * 13 + 3 <= 64, "barrier block fits in 512 bytes");
   static_assert(K_BYTES + V_BYTES == 16384, "k|v buffer holds one 32-column fp32 chunk of x");
 };
@@ -86,6 +88,8 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* mma_done = bars + 4 + 2 * FB_COUNT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 2);
+  // bo | ln2_w | ln2_b, read by every row thread in the out-projection epilogue.
+  float* sprm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);
   auto sb = [&](int s, int i) { return bars + 4 + FB_COUNT * s + i; };
   auto slot_a = [&](int s) { return sSlot + s * C::SLOT; };
   auto slot_c = [&](int s) { return sSlot + s * C::SLOT + C::A_BYTES; };
@@ -123,6 +127,11 @@ __global__ void __launch_bounds__(512, 1)
     tma_prefetch_desc(&map_wo);
     tma_prefetch_desc(&map_x);
     tma_prefetch_desc(&map_y);
+  }
+  for (int i = threadIdx.x; i < DM; i += blockDim.x) {
+    sprm[i] = a.bo[i];
+    sprm[DM + i] = a.ln2_w[i];
+    sprm[2 * DM + i] = a.ln2_b[i];
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -253,11 +262,16 @@ __global__ void __launch_bounds__(512, 1)
     const int rbeg = ((warp - 12) & 1) * 64;
     const uint32_t a_base = smem_u32(slot_a(s));
     const float inv_d = 1.0f / (float)DM;
-    const int k = lane * 4;
-    float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = w4;
-    if (k < DM) {
-      w4 = __ldg(reinterpret_cast<const float4*>(a.ln1_w + k));
-      b4 = __ldg(reinterpret_cast<const float4*>(a.ln1_b + k));
+    // Eight lanes per row, four rows per warp instruction: lane (grp, l) holds
+    // columns 32*m + 4*l (m < NV) of row 4*i + grp, so every load instruction
+    // reads four 128-byte segments and a row reduces in three shuffle steps.
+    constexpr int NV = DM / 32;               // float4 per lane per row
+    const int grp = lane >> 3, l8 = lane & 7;
+    float4 w4[NV], b4[NV];
+#pragma unroll
+    for (int m = 0; m < NV; ++m) {
+      w4[m] = __ldg(reinterpret_cast<const float4*>(a.ln1_w + 32 * m + 4 * l8));
+      b4[m] = __ldg(reinterpret_cast<const float4*>(a.ln1_b + 32 * m + 4 * l8));
     }
     int pi = 0;
     for (int pair = blockIdx.x; pair < npairs; pair += gridDim.x, ++pi) {
@@ -275,48 +289,56 @@ __global__ void __launch_bounds__(512, 1)
       }
       // A of this slot is free once the previous sequence's last projection was read.
       if (!mbar_wait(sb(s, FB_A_FREE), (pi & 1) ^ 1, abort_flag)) break;
-      constexpr int LNB = 16;   // rows per batch: 16 coalesced row loads in flight per warp
+      constexpr int IT = 2;   // row groups per batch: 8 rows, 2*NV loads in flight per lane
 #pragma unroll 1
-      for (int r0 = rbeg; r0 < rbeg + 64; r0 += LNB) {
-        float4 v[LNB];
+      for (int r0 = rbeg; r0 < rbeg + 64; r0 += 4 * IT) {
+        float4 v[IT][NV];
 #pragma unroll
-        for (int j = 0; j < LNB; ++j) {
-          v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (r0 + j < S && k < DM) v[j] = __ldg(reinterpret_cast<const float4*>(a.x + (t0 + r0 + j) * DM + k));
+        for (int it = 0; it < IT; ++it) {
+          const int r = r0 + 4 * it + grp;
+#pragma unroll
+          for (int m = 0; m < NV; ++m)
+            v[it][m] = (r < S) ? ldg_stream_f4(a.x + (t0 + r) * DM + 32 * m + 4 * l8)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        // LNB rows reduced together: each xor-shuffle step has LNB independent
-        // shuffles in flight instead of one dependent chain per row.
-        float red[LNB];
+        float red[IT], mean[IT], rstd[IT];
 #pragma unroll
-        for (int j = 0; j < LNB; ++j) red[j] = (v[j].x + v[j].y) + (v[j].z + v[j].w);
+        for (int it = 0; it < IT; ++it) {
+          float sm = 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
+          for (int m = 0; m < NV; ++m) sm += (v[it][m].x + v[it][m].y) + (v[it][m].z + v[it][m].w);
+          red[it] = sm;
+        }
 #pragma unroll
-          for (int j = 0; j < LNB; ++j) red[j] += __shfl_xor_sync(0xffffffffu, red[j], o);
-        float mean[LNB];
+        for (int o = 1; o < 8; o <<= 1)
 #pragma unroll
-        for (int j = 0; j < LNB; ++j) {
-          mean[j] = red[j] * inv_d;
+          for (int it = 0; it < IT; ++it) red[it] += __shfl_xor_sync(0xffffffffu, red[it], o);
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+          mean[it] = red[it] * inv_d;
           float sq = 0.f;
-          if (k < DM) {
-            const float e0 = v[j].x - mean[j], e1 = v[j].y - mean[j], e2 = v[j].z - mean[j], e3 = v[j].w - mean[j];
-            sq = (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
+#pragma unroll
+          for (int m = 0; m < NV; ++m) {
+            v[it][m].x -= mean[it]; v[it][m].y -= mean[it]; v[it][m].z -= mean[it]; v[it][m].w -= mean[it];
+            sq += (v[it][m].x * v[it][m].x + v[it][m].y * v[it][m].y) + (v[it][m].z * v[it][m].z + v[it][m].w * v[it][m].w);
           }
-          red[j] = sq;
+          red[it] = sq;
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
+        for (int o = 1; o < 8; o <<= 1)
 #pragma unroll
-          for (int j = 0; j < LNB; ++j) red[j] += __shfl_xor_sync(0xffffffffu, red[j], o);
+          for (int it = 0; it < IT; ++it) red[it] += __shfl_xor_sync(0xffffffffu, red[it], o);
 #pragma unroll
-        for (int j = 0; j < LNB; ++j) {
-          const int r = r0 + j;
-          const float rstd = rsqrtf(red[j] * inv_d + a.eps1);
-          if (k < DM) {
+        for (int it = 0; it < IT; ++it) {
+          rstd[it] = rsqrtf(red[it] * inv_d + a.eps1);
+          const int r = r0 + 4 * it + grp;
+#pragma unroll
+          for (int m = 0; m < NV; ++m) {
+            const int k = 32 * m + 4 * l8;
             uint32_t lo = 0, hi = 0;
             if (r < S) {
-              lo = pack_half2((v[j].x - mean[j]) * rstd * w4.x + b4.x, (v[j].y - mean[j]) * rstd * w4.y + b4.y);
-              hi = pack_half2((v[j].z - mean[j]) * rstd * w4.z + b4.z, (v[j].w - mean[j]) * rstd * w4.w + b4.w);
+              lo = pack_half2(v[it][m].x * rstd[it] * w4[m].x + b4[m].x, v[it][m].y * rstd[it] * w4[m].y + b4[m].y);
+              hi = pack_half2(v[it][m].z * rstd[it] * w4[m].z + b4[m].z, v[it][m].w * rstd[it] * w4[m].w + b4[m].w);
             }
             st_shared_v2(a_base + (k >> 6) * 16384 + swz_offset(r, (k & 63) >> 3, 128) + (k & 7) * 2, lo, hi);
           }
@@ -556,7 +578,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const int col = cc * 32 + 4 * c;
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bo + col));
+            const float4 bb = *reinterpret_cast<const float4*>(sprm + col);
             const float a0 = xv[4 * c + 0] + (qkeep ? __uint_as_float(r[4 * c + 0]) + bb.x : 0.f);
             const float a1 = xv[4 * c + 1] + (qkeep ? __uint_as_float(r[4 * c + 1]) + bb.y : 0.f);
             const float a2 = xv[4 * c + 2] + (qkeep ? __uint_as_float(r[4 * c + 2]) + bb.z : 0.f);
@@ -578,36 +600,46 @@ __global__ void __launch_bounds__(512, 1)
         const float dmean = sum * inv_d;
         const float mean = shift + dmean;
         const float rstd = rsqrtf(fmaxf(sumsq * inv_d - dmean * dmean, 0.f) + a.eps2);
-        // y leaves one 32-column fp32 atom (16 KB, 128-byte swizzle) at a time
-        // through free buffers -- the two halves of ctx, then k|v -- by TMA
-        // store (rows >= S are clipped); a buffer is reused only after TMA has
-        // read it.
-#pragma unroll 1
-        for (int cc = 0; cc < NXC; ++cc) {
-          // chunk -> staging buffer: 0 ctx half 0, 1 ctx half 1, 2 k|v, 3 ctx half 0 again
-          uint8_t* ybuf = (cc == 2) ? xbuf : (cbuf + (cc == 1 ? 16384 : 0));
-          if (cc == 3) {   // ctx half 0 again: y chunk 0's store must have read it
-            if (leader) bulk_wait_read<2>();
-            named_bar_sync(1 + s, 128);
-          }
+        // y leaves in 32-column fp32 atoms (16 KB, 128-byte swizzle) by TMA
+        // store (rows >= S are clipped): chunks 0-2 through the two halves of
+        // ctx and the k|v buffer in one round, then chunk 3 through ctx half 0
+        // once TMA has read chunk 0 from it.
+        auto write_y = [&](int cc, uint8_t* ybuf) {
           uint32_t r[32];
           tmem_ld32(tb + 32 * cc, r);
           const uint32_t dst = smem_u32(ybuf) + row * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const int col = cc * 32 + 4 * c;
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(a.ln2_w + col));
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(a.ln2_b + col));
+            const float4 wv = *reinterpret_cast<const float4*>(sprm + DM + col);
+            const float4 bb = *reinterpret_cast<const float4*>(sprm + 2 * DM + col);
             st_shared_v4(dst + ((c ^ (row & 7)) << 4),
                          __float_as_uint((__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bb.x),
                          __float_as_uint((__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bb.y),
                          __float_as_uint((__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bb.z),
                          __float_as_uint((__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bb.w));
           }
+        };
+        constexpr int NY0 = NXC < 3 ? NXC : 3;            // chunks in the first round
+        write_y(0, cbuf);
+        write_y(1, cbuf + 16384);
+        if (NY0 > 2) write_y(2, xbuf);
+        fence_proxy_async_smem();
+        named_bar_sync(1 + s, 128);
+        if (leader) {
+          for (int cc = 0; cc < NY0; ++cc) {
+            tma_store_3d(&map_y, cc == 2 ? xbuf : cbuf + cc * 16384, cc * 32, 0, seq);
+            bulk_commit();
+          }
+        }
+        if (NXC > 3) {
+          if (leader) bulk_wait_read<2>();   // chunk 0 (ctx half 0) has been read
+          named_bar_sync(1 + s, 128);
+          write_y(3, cbuf);
           fence_proxy_async_smem();
           named_bar_sync(1 + s, 128);
           if (leader) {
-            tma_store_3d(&map_y, ybuf, cc * 32, 0, seq);
+            tma_store_3d(&map_y, cbuf, 96, 0, seq);
             bulk_commit();
           }
         }
