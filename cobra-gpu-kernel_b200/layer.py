@@ -122,6 +122,7 @@ class B200TransformerLayer(nn.Module):
         self._static_m = None
         self._host_out = None
         self._io_streams = None
+        self._warm = set()
         self.register_load_state_dict_post_hook(lambda mod, _keys: mod.invalidate())
 
     @classmethod
@@ -139,7 +140,10 @@ class B200TransformerLayer(nn.Module):
         self._sig = None
 
     def _param_versions(self):
-        return tuple(p._version for p in self.parameters())
+        # Parameters created under torch.inference_mode() carry no version
+        # counter; their storage address still identifies a replaced tensor
+        # (in-place edits of such weights need an explicit invalidate()).
+        return tuple((p.data_ptr(), 0 if p.is_inference() else p._version) for p in self.parameters())
 
     def _ensure_pack(self, device: torch.device) -> _Pack:
         pk = self._pack
@@ -257,6 +261,27 @@ class B200TransformerLayer(nn.Module):
             y = torch.empty_like(x)
             self._launch(x, y, desc)
             return y
+
+    def warmup(self, seq_len: int, device: torch.device, with_mask: bool = False) -> None:
+        """Pack the weights and run one single-sequence forward of this shape
+        class on ``device`` (zeros), so that the kernels it launches are
+        loaded before the caller starts other device work -- e.g. NCCL
+        transfers in flight, which a lazily loaded kernel must not wait on.
+        Runs once per (seq_len, device, mask) combination."""
+        key = (int(seq_len), torch.device(device), bool(with_mask))
+        if key in self._warm:
+            return
+        d = self.attention.d_model
+        x = torch.zeros(1, seq_len, d, dtype=torch.float32, device=device)
+        m = torch.ones(1, seq_len, dtype=torch.bool, device=device) if with_mask else None
+        saved, self.use_graphs = self.use_graphs, False
+        try:
+            with torch.inference_mode():
+                self.forward(x, m)
+            torch.cuda.current_stream(device).synchronize()
+        finally:
+            self.use_graphs = saved
+        self._warm.add(key)
 
     def _forward_host(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
         """Host x -> host y through the GPU that holds the parameters.

@@ -123,6 +123,12 @@ def sharded_forward(layer: Callable[..., torch.Tensor], x: Optional[torch.Tensor
     if status != _HDR_OK:
         raise ValueError(f"sharded_forward: {_HDR_MESSAGES[status]} (validated on rank {src})")
 
+    # Before any transfer is posted: a layer that can warm up packs its
+    # weights and loads its kernels now, so that no first-use work (weight
+    # packing, lazy kernel loading) waits behind NCCL kernels in flight.
+    warm = getattr(layer, "warmup", None)
+    if warm is not None and batch_shards(B, world)[rank][1] > batch_shards(B, world)[rank][0]:
+        warm(S, device, bool(has_mask))
     # Run the layer eagerly while transfers are in flight: a CUDA-graph
     # capture (B200TransformerLayer captures on the first call per shape, and
     # ragged chunks change the shape) must not overlap NCCL work.

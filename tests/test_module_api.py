@@ -39,3 +39,17 @@ def test_load_state_dict_invalidates_pack(pkg):
     lay._pack = object()
     lay.load_state_dict(ReferenceLayer(64, 2).state_dict())
     assert lay._pack is None
+
+
+def test_module_built_under_inference_mode_tracks_parameters(pkg):
+    """A layer constructed inside torch.inference_mode() has inference-tensor
+    parameters (no version counter); weight-change tracking must still work."""
+    import torch
+    with torch.inference_mode():
+        lay = pkg.B200TransformerLayer(64, 2)
+        v1 = lay._param_versions()
+    v2 = lay._param_versions()
+    assert v1 == v2
+    with torch.inference_mode():
+        lay.norm1.weight = torch.nn.Parameter(torch.ones(64))
+    assert lay._param_versions() != v1

@@ -56,6 +56,7 @@ def _worker(rank: int, world: int, port: int, root: str) -> None:
                 layer.load_state_dict(ref.state_dict(), strict=True)
                 x, _ = generate_random_case(cfg, seed=22)
                 x = x.to(dev)
+                print(f"rank {rank}: case {(B, S, d, H, causal, chunks)}", flush=True)
                 y = pkg.sharded_forward(layer, x if rank == 0 else None, chunks=chunks)
                 torch.cuda.synchronize(dev)
                 layer.check_status()
@@ -66,8 +67,16 @@ def _worker(rank: int, world: int, port: int, root: str) -> None:
                 else:
                     assert y is None
         dist.barrier()
-    finally:
         dist.destroy_process_group()
+    except BaseException:
+        # Leave at once: a rank that failed with transfers in flight must not
+        # wait in destroy_process_group for peers that will never answer.
+        import os
+        import traceback
+        traceback.print_exc()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(1)
 
 
 def test_sharded_forward_two_gpus_bitwise(pkg):
