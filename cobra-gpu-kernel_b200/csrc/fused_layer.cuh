@@ -397,8 +397,12 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float4 bb = __ldg(bq + i);
-            pk[2 * i] = pack_half2(__uint_as_float(r[4 * i]) + bb.x, __uint_as_float(r[4 * i + 1]) + bb.y);
-            pk[2 * i + 1] = pack_half2(__uint_as_float(r[4 * i + 2]) + bb.z, __uint_as_float(r[4 * i + 3]) + bb.w);
+            const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                          make_float2(bb.x, bb.y));
+            const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                          make_float2(bb.z, bb.w));
+            pk[2 * i] = pack_half2(v01.x, v01.y);
+            pk[2 * i + 1] = pack_half2(v23.x, v23.y);
           }
           tmem_st16(tb + 96, pk);
           tmem_ld32(tb + 32, r);
@@ -406,8 +410,12 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float4 bb = __ldg(bk + i);
-            pk[2 * i] = pack_half2(__uint_as_float(r[4 * i]) + bb.x, __uint_as_float(r[4 * i + 1]) + bb.y);
-            pk[2 * i + 1] = pack_half2(__uint_as_float(r[4 * i + 2]) + bb.z, __uint_as_float(r[4 * i + 3]) + bb.w);
+            const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                          make_float2(bb.x, bb.y));
+            const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                          make_float2(bb.z, bb.w));
+            pk[2 * i] = pack_half2(v01.x, v01.y);
+            pk[2 * i + 1] = pack_half2(v23.x, v23.y);
           }
 #pragma unroll
           for (int c = 0; c < 4; ++c)
@@ -420,8 +428,11 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float4 bb = __ldg(bv + i);
-            const float vv[4] = {__uint_as_float(r[4 * i]) + bb.x, __uint_as_float(r[4 * i + 1]) + bb.y,
-                                 __uint_as_float(r[4 * i + 2]) + bb.z, __uint_as_float(r[4 * i + 3]) + bb.w};
+            const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                          make_float2(bb.x, bb.y));
+            const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                          make_float2(bb.z, bb.w));
+            const float vv[4] = {v01.x, v01.y, v23.x, v23.y};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int j = 4 * i + e;
@@ -496,16 +507,17 @@ __global__ void __launch_bounds__(512, 1)
           uint32_t r[32];
           tmem_ld32(tb + 96, r);
           const float il = l > 0.f ? 1.0f / l : 0.f;
+          const float2 il2 = make_float2(il, il);
           const int col0 = 32 * h;
           const uint32_t cb = c_base + (uint32_t)(col0 >> 6) * 16384 + row * 128;
           const int ch0 = (col0 & 63) >> 3;
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             st_shared_v4(cb + (((ch0 + c) ^ (row & 7)) << 4),
-                         pack_half2(__uint_as_float(r[8 * c + 0]) * il, __uint_as_float(r[8 * c + 1]) * il),
-                         pack_half2(__uint_as_float(r[8 * c + 2]) * il, __uint_as_float(r[8 * c + 3]) * il),
-                         pack_half2(__uint_as_float(r[8 * c + 4]) * il, __uint_as_float(r[8 * c + 5]) * il),
-                         pack_half2(__uint_as_float(r[8 * c + 6]) * il, __uint_as_float(r[8 * c + 7]) * il));
+                         pack_f2h(__fmul2_rn(make_float2(__uint_as_float(r[8 * c + 0]), __uint_as_float(r[8 * c + 1])), il2)),
+                         pack_f2h(__fmul2_rn(make_float2(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3])), il2)),
+                         pack_f2h(__fmul2_rn(make_float2(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5])), il2)),
+                         pack_f2h(__fmul2_rn(make_float2(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7])), il2)));
         }
       }
       if (!ok) break;
@@ -540,7 +552,8 @@ __global__ void __launch_bounds__(512, 1)
         // Statistics in one pass over the shifted values r - r0 (r0 = the row's
         // first element): var = E[(r-r0)^2] - E[r-r0]^2 has no cancellation when
         // the row's spread is small next to its mean.
-        float shift = 0.f, sum = 0.f, sumsq = 0.f;
+        float shift = 0.f;
+        float2 sum2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);   // packed fp32x2 partials
         bool xok = true;
 #pragma unroll 1
         for (int cc = 0; cc < NXC; ++cc) {
@@ -579,27 +592,36 @@ __global__ void __launch_bounds__(512, 1)
           for (int c = 0; c < 8; ++c) {
             const int col = cc * 32 + 4 * c;
             const float4 bb = *reinterpret_cast<const float4*>(sprm + col);
-            const float a0 = xv[4 * c + 0] + (qkeep ? __uint_as_float(r[4 * c + 0]) + bb.x : 0.f);
-            const float a1 = xv[4 * c + 1] + (qkeep ? __uint_as_float(r[4 * c + 1]) + bb.y : 0.f);
-            const float a2 = xv[4 * c + 2] + (qkeep ? __uint_as_float(r[4 * c + 2]) + bb.z : 0.f);
-            const float a3 = xv[4 * c + 3] + (qkeep ? __uint_as_float(r[4 * c + 3]) + bb.w : 0.f);
-            if (cc == 0 && c == 0) shift = a0;
-            const float d0 = a0 - shift, d1 = a1 - shift, d2 = a2 - shift, d3 = a3 - shift;
-            sum += (d0 + d1) + (d2 + d3);
-            sumsq += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
-            r[4 * c + 0] = __float_as_uint(a0);
-            r[4 * c + 1] = __float_as_uint(a1);
-            r[4 * c + 2] = __float_as_uint(a2);
-            r[4 * c + 3] = __float_as_uint(a3);
+            // r = x + (acc + bo), in pairs; a padded row keeps r = x.
+            float2 a01 = make_float2(xv[4 * c + 0], xv[4 * c + 1]);
+            float2 a23 = make_float2(xv[4 * c + 2], xv[4 * c + 3]);
+            if (qkeep) {
+              a01 = __fadd2_rn(a01, __fadd2_rn(make_float2(__uint_as_float(r[4 * c + 0]), __uint_as_float(r[4 * c + 1])),
+                                               make_float2(bb.x, bb.y)));
+              a23 = __fadd2_rn(a23, __fadd2_rn(make_float2(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])),
+                                               make_float2(bb.z, bb.w)));
+            }
+            if (cc == 0 && c == 0) shift = a01.x;
+            const float2 nsh = make_float2(-shift, -shift);
+            const float2 d01 = __fadd2_rn(a01, nsh), d23 = __fadd2_rn(a23, nsh);
+            sum2 = __fadd2_rn(sum2, __fadd2_rn(d01, d23));
+            sq2 = __ffma2_rn(d01, d01, sq2);
+            sq2 = __ffma2_rn(d23, d23, sq2);
+            r[4 * c + 0] = __float_as_uint(a01.x);
+            r[4 * c + 1] = __float_as_uint(a01.y);
+            r[4 * c + 2] = __float_as_uint(a23.x);
+            r[4 * c + 3] = __float_as_uint(a23.y);
           }
           tmem_st32(tb + 32 * cc, r);
         }
         fence_proxy_async_smem();     // x reads before the TMA stores that reuse the buffers
         named_bar_sync(1 + s, 128);   // all x chunks read: their buffers take y
         if (!xok) break;
-        const float dmean = sum * inv_d;
+        const float dmean = (sum2.x + sum2.y) * inv_d;
         const float mean = shift + dmean;
-        const float rstd = rsqrtf(fmaxf(sumsq * inv_d - dmean * dmean, 0.f) + a.eps2);
+        const float rstd = rsqrtf(fmaxf((sq2.x + sq2.y) * inv_d - dmean * dmean, 0.f) + a.eps2);
+        // y = (r - mean) * rstd * w + b as (r * rstd - mean * rstd) * w + b, in pairs.
+        const float2 rs2 = make_float2(rstd, rstd), nm2 = make_float2(-mean * rstd, -mean * rstd);
         // y leaves in 32-column fp32 atoms (16 KB, 128-byte swizzle) by TMA
         // store (rows >= S are clipped): chunks 0-2 through the two halves of
         // ctx and the k|v buffer in one round, then chunk 3 through ctx half 0
@@ -613,11 +635,12 @@ __global__ void __launch_bounds__(512, 1)
             const int col = cc * 32 + 4 * c;
             const float4 wv = *reinterpret_cast<const float4*>(sprm + DM + col);
             const float4 bb = *reinterpret_cast<const float4*>(sprm + 2 * DM + col);
-            st_shared_v4(dst + ((c ^ (row & 7)) << 4),
-                         __float_as_uint((__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bb.x),
-                         __float_as_uint((__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bb.y),
-                         __float_as_uint((__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bb.z),
-                         __float_as_uint((__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bb.w));
+            const float2 t01 = __ffma2_rn(make_float2(__uint_as_float(r[4 * c + 0]), __uint_as_float(r[4 * c + 1])), rs2, nm2);
+            const float2 t23 = __ffma2_rn(make_float2(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])), rs2, nm2);
+            const float2 y01 = __ffma2_rn(t01, make_float2(wv.x, wv.y), make_float2(bb.x, bb.y));
+            const float2 y23 = __ffma2_rn(t23, make_float2(wv.z, wv.w), make_float2(bb.z, bb.w));
+            st_shared_v4(dst + ((c ^ (row & 7)) << 4), __float_as_uint(y01.x), __float_as_uint(y01.y),
+                         __float_as_uint(y23.x), __float_as_uint(y23.y));
           }
         };
         constexpr int NY0 = NXC < 3 ? NXC : 3;            // chunks in the first round
