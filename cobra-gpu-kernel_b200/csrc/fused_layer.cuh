@@ -64,12 +64,15 @@ struct FusedCfg {
   static constexpr int PARAM_BYTES = 3 * DM * 4;     // bo, ln2_w, ln2_b in shared memory
   static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + PARAM_BYTES + 1024;
   static_assert(SMEM <= 232448, "fits the 227 KB opt-in shared memory of one CTA");
-  static_assert(4 + 2 * 13 + 3 <= 64, "barrier block fits in 512 bytes");
+  static_assert(4 + 2 * 14 + 4 <= 64, "barrier block fits in 512 bytes");
+  // d = 128: the fourth 32-column chunk of x and y is staged in the weight
+  // buffer that held Wo, once both slots' out-projections have read it.
+  static constexpr bool WO_STAGE = DM / 32 > 3;
   static_assert(K_BYTES + V_BYTES == 16384, "k|v buffer holds one 32-column fp32 chunk of x");
 };
 
 enum FusedBar : int { FB_A_READY = 0, FB_A_FREE, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY,
-                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_X0, FB_X1, FB_X2, FB_COUNT };
+                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_X0, FB_X1, FB_X2, FB_X3, FB_COUNT };
 
 template <int DM, bool KMASK>   // KMASK: a key-padding mask may be given
 __global__ void __launch_bounds__(512, 1)
@@ -88,6 +91,7 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* mma_done = bars + 4 + 2 * FB_COUNT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 2);
+  uint64_t* wo_done = mma_done + 3;   // both slots' out-projections have read Wo
   // bo | ln2_w | ln2_b, read by every row thread in the out-projection epilogue.
   float* sprm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);
   auto sb = [&](int s, int i) { return bars + 4 + FB_COUNT * s + i; };
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(512, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(sb(s, FB_A_READY), 2);
-      mbar_init(sb(s, FB_A_FREE), 4);
+      mbar_init(sb(s, FB_A_FREE), 1);
       mbar_init(sb(s, FB_QKV_FULL), 1);
       mbar_init(sb(s, FB_QKV_FREE), 4);
       mbar_init(sb(s, FB_KQV_READY), 4);
@@ -119,8 +123,10 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(sb(s, FB_X0), 1);
       mbar_init(sb(s, FB_X1), 1);
       mbar_init(sb(s, FB_X2), 1);
+      mbar_init(sb(s, FB_X3), 1);
     }
     mbar_init(mma_done, 2);
+    mbar_init(wo_done, 2);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&map_wqkv);
@@ -199,6 +205,9 @@ __global__ void __launch_bounds__(512, 1)
                         k > 0 ? 1u : 0u);
           }
           umma_commit(sb(s, FB_QKV_FULL));
+          // The last projection of the sequence is the last reader of A: LN1
+          // may refill it as soon as that MMA completes.
+          if (h == H - 1) umma_commit(sb(s, FB_A_FREE));
         }
         umma_commit(&w_empty[b]);
         ++wt;
@@ -250,7 +259,10 @@ __global__ void __launch_bounds__(512, 1)
             }
             umma_commit(sb(s, FB_OUT_FULL));
           }
-          umma_commit(&w_empty[b]);
+          // With WO_STAGE the row leaders release this buffer after staging
+          // x / y chunk 3 in it.
+          if constexpr (C::WO_STAGE) umma_commit(wo_done);
+          else umma_commit(&w_empty[b]);
           ++wt;
         }
       }
@@ -363,6 +375,11 @@ __global__ void __launch_bounds__(512, 1)
       const int seq = 2 * pair + s;
       if (seq >= a.B) break;
       const long long t0 = (long long)seq * S;
+      const bool leader = (q == 0 && lane == 0);
+      if (pi > 0) {   // the previous sequence's y stores have read k|v, ctx
+        if (leader) bulk_wait_read_all();
+        named_bar_sync(1 + s, 128);
+      }
       // Keys this row may see, one bit each: valid (mask), inside S, causal.
       // A padded query row (mask byte 0) keeps y = LN2(x): its attention
       // output, bias included, is zeroed (BaselineSelfAttention :106-109, :121-122).
@@ -444,8 +461,7 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if (h < H - 1) mbar_arrive(sb(s, FB_QKV_FREE));
-          else mbar_arrive(sb(s, FB_A_FREE));   // last projection of this sequence has read A
+          if (h < H - 1) mbar_arrive(sb(s, FB_QKV_FREE));   // the last head's is arrived after LN2
           mbar_arrive(sb(s, FB_KQV_READY));
         }
         // ---- softmax of S = q k^T (one row per thread, exact: S <= 128 keys)
@@ -529,12 +545,17 @@ __global__ void __launch_bounds__(512, 1)
       // The residual x arrives by TMA as 128-row x 32-column fp32 chunks (16 KB,
       // 128-byte swizzle): chunk 0 into the k|v buffer (free since the last
       // P v), chunks 1-2 into the two halves of ctx once the out-projection has
-      // read it, chunk 3 into k|v again once chunk 0 is consumed.
+      // read it, chunk 3 (d = 128) into this slot's half of the weight buffer
+      // that held Wo, once both slots' out-projections have read it. y leaves
+      // through the same four buffers.
       constexpr int NXC = DM / 32;                       // 4 (d=128) or 2 (d=64)
-      const bool leader = (q == 0 && lane == 0);
       uint8_t* xbuf = slot_k(s);
       uint8_t* cbuf = slot_c(s);
-      const int x0_uses = (NXC + 2) / 3;                 // chunks 0 and 3 share k|v
+      const int wo_b = (pi * (H + 1) + H) & 1;           // ring buffer of this pair's Wo tile
+      uint8_t* wbuf = sW + wo_b * C::WBUF + s * 16384;
+      auto xchunk = [&](int cc) -> uint8_t* {
+        return cc == 0 ? xbuf : (cc == 3 ? wbuf : cbuf + (cc - 1) * 16384);
+      };
       if (leader) {
         mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
         tma_load_3d(xbuf, &map_x, sb(s, FB_X0), 0, 0, seq);
@@ -545,7 +566,13 @@ __global__ void __launch_bounds__(512, 1)
         for (int cc = 1; cc < NXC && cc < 3; ++cc) {
           uint64_t* bar = sb(s, cc == 1 ? FB_X1 : FB_X2);
           mbar_arrive_expect_tx(bar, 16384);
-          tma_load_3d(cbuf + (cc - 1) * 16384, &map_x, bar, cc * 32, 0, seq);
+          tma_load_3d(xchunk(cc), &map_x, bar, cc * 32, 0, seq);
+        }
+        if constexpr (C::WO_STAGE) {
+          if (mbar_wait(wo_done, pi & 1, abort_flag)) {
+            mbar_arrive_expect_tx(sb(s, FB_X3), 16384);
+            tma_load_3d(wbuf, &map_x, sb(s, FB_X3), 96, 0, seq);
+          }
         }
       }
       {
@@ -557,34 +584,14 @@ __global__ void __launch_bounds__(512, 1)
         bool xok = true;
 #pragma unroll 1
         for (int cc = 0; cc < NXC; ++cc) {
-          uint64_t* bar;
-          uint32_t par;
-          const uint8_t* src;
-          if (cc == 0 || cc == 3) {
-            bar = sb(s, FB_X0);
-            par = (uint32_t)(pi * x0_uses + (cc == 3 ? 1 : 0)) & 1;
-            src = xbuf;
-          } else {
-            bar = sb(s, cc == 1 ? FB_X1 : FB_X2);
-            par = (uint32_t)pi & 1;
-            src = cbuf + (cc - 1) * 16384;
-          }
-          if (!mbar_wait(bar, par, abort_flag)) { xok = false; break; }
+          uint64_t* bar = sb(s, FB_X0 + cc);
+          const uint8_t* src = xchunk(cc);
+          if (!mbar_wait(bar, pi & 1, abort_flag)) { xok = false; break; }
           float xv[32];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float4 t4 = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
             xv[4 * c + 0] = t4.x; xv[4 * c + 1] = t4.y; xv[4 * c + 2] = t4.z; xv[4 * c + 3] = t4.w;
-          }
-          if (cc == 0 && NXC > 3) {   // every row has read chunk 0: k|v takes chunk 3
-            // The TMA write that follows is in the async proxy: order this thread's
-            // generic reads of the buffer before it (a plain bar.sync does not).
-            fence_proxy_async_smem();
-            named_bar_sync(1 + s, 128);
-            if (leader) {
-              mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
-              tma_load_3d(xbuf, &map_x, sb(s, FB_X0), 96, 0, seq);
-            }
           }
           uint32_t r[32];
           tmem_ld32(tb + 32 * cc, r);
@@ -623,9 +630,8 @@ __global__ void __launch_bounds__(512, 1)
         // y = (r - mean) * rstd * w + b as (r * rstd - mean * rstd) * w + b, in pairs.
         const float2 rs2 = make_float2(rstd, rstd), nm2 = make_float2(-mean * rstd, -mean * rstd);
         // y leaves in 32-column fp32 atoms (16 KB, 128-byte swizzle) by TMA
-        // store (rows >= S are clipped): chunks 0-2 through the two halves of
-        // ctx and the k|v buffer in one round, then chunk 3 through ctx half 0
-        // once TMA has read chunk 0 from it.
+        // store (rows >= S are clipped), each through the buffer its x chunk
+        // came in, all in one round.
         auto write_y = [&](int cc, uint8_t* ybuf) {
           uint32_t r[32];
           tmem_ld32(tb + 32 * cc, r);
@@ -643,32 +649,24 @@ __global__ void __launch_bounds__(512, 1)
                          __float_as_uint(y23.x), __float_as_uint(y23.y));
           }
         };
-        constexpr int NY0 = NXC < 3 ? NXC : 3;            // chunks in the first round
-        write_y(0, cbuf);
-        write_y(1, cbuf + 16384);
-        if (NY0 > 2) write_y(2, xbuf);
+#pragma unroll 1
+        for (int cc = 0; cc < NXC; ++cc) write_y(cc, xchunk(cc));
         fence_proxy_async_smem();
         named_bar_sync(1 + s, 128);
         if (leader) {
-          for (int cc = 0; cc < NY0; ++cc) {
-            tma_store_3d(&map_y, cc == 2 ? xbuf : cbuf + cc * 16384, cc * 32, 0, seq);
+          if constexpr (C::WO_STAGE) {   // chunk 3 first, in its own group: it frees the weight buffer
+            tma_store_3d(&map_y, wbuf, 96, 0, seq);
             bulk_commit();
           }
-        }
-        if (NXC > 3) {
-          if (leader) bulk_wait_read<2>();   // chunk 0 (ctx half 0) has been read
-          named_bar_sync(1 + s, 128);
-          write_y(3, cbuf);
-          fence_proxy_async_smem();
-          named_bar_sync(1 + s, 128);
-          if (leader) {
-            tma_store_3d(&map_y, cbuf, 96, 0, seq);
-            bulk_commit();
+          for (int cc = 0; cc < NXC && cc < 3; ++cc) tma_store_3d(&map_y, xchunk(cc), cc * 32, 0, seq);
+          bulk_commit();
+          if constexpr (C::WO_STAGE) {
+            bulk_wait_read<1>();
+            mbar_arrive(&w_empty[wo_b]);
           }
         }
-        // ctx and k|v are rewritten by the next sequence: wait until TMA has read them.
-        if (leader) bulk_wait_read_all();
-        named_bar_sync(1 + s, 128);
+        // ctx and k|v are rewritten by the next sequence: the leader waits for
+        // TMA to have read them at the start of that sequence.
       }
       tc_fence_before();
       __syncwarp();
