@@ -113,6 +113,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// mbar_wait by all 32 lanes of a converged warp, with one verdict for the
+// whole warp: a warp-collective instruction after it (tcgen05.ld/st) never
+// runs with part of the warp gone.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+}
+
 // Wait used only while unwinding: ignores the abort flag, bounded by time.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();

@@ -64,7 +64,7 @@ struct FusedCfg {
   static constexpr int PARAM_BYTES = 3 * DM * 4;     // bo, ln2_w, ln2_b in shared memory
   static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + PARAM_BYTES + 1024;
   static_assert(SMEM <= 232448, "fits the 227 KB opt-in shared memory of one CTA");
-  static_assert(4 + 2 * 14 + 4 <= 64, "barrier block fits in 512 bytes");
+  static_assert(4 + 2 * 16 + 4 <= 64, "barrier block fits in 512 bytes");
   // d = 128: the fourth 32-column chunk of x and y is staged in the weight
   // buffer that held Wo, once both slots' out-projections have read it.
   static constexpr bool WO_STAGE = DM / 32 > 3;
@@ -72,7 +72,8 @@ struct FusedCfg {
 };
 
 enum FusedBar : int { FB_A_READY = 0, FB_A_FREE, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY,
-                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_X0, FB_X1, FB_X2, FB_X3, FB_COUNT };
+                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_X0, FB_X1, FB_X2, FB_X3,
+                      FB_Y_STAGED, FB_Y_READ, FB_COUNT };
 
 template <int DM, bool KMASK>   // KMASK: a key-padding mask may be given
 __global__ void __launch_bounds__(512, 1)
@@ -124,6 +125,8 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(sb(s, FB_X1), 1);
       mbar_init(sb(s, FB_X2), 1);
       mbar_init(sb(s, FB_X3), 1);
+      mbar_init(sb(s, FB_Y_STAGED), 4);   // every row warp has written its y rows
+      mbar_init(sb(s, FB_Y_READ), 1);     // the leader saw TMA finish reading them
     }
     mbar_init(mma_done, 2);
     mbar_init(wo_done, 2);
@@ -376,9 +379,12 @@ __global__ void __launch_bounds__(512, 1)
       if (seq >= a.B) break;
       const long long t0 = (long long)seq * S;
       const bool leader = (q == 0 && lane == 0);
-      if (pi > 0) {   // the previous sequence's y stores have read k|v, ctx
-        if (leader) bulk_wait_read_all();
-        named_bar_sync(1 + s, 128);
+      if (pi > 0) {   // the previous sequence's y stores must have read k|v and ctx
+        if (leader) {
+          bulk_wait_read_all();
+          mbar_arrive(sb(s, FB_Y_READ));
+        }
+        if (!mbar_wait_warp(sb(s, FB_Y_READ), (pi - 1) & 1, abort_flag)) break;
       }
       // Keys this row may see, one bit each: valid (mask), inside S, causal.
       // A padded query row (mask byte 0) keeps y = LN2(x): its attention
@@ -405,7 +411,7 @@ __global__ void __launch_bounds__(512, 1)
       for (int h = 0; h < H; ++h) {
         const int n = pi * H + h;
         // ---- q|k|v of head h: bias, fp16; q -> TMEM, k and v^T -> shared memory
-        if (!mbar_wait(sb(s, FB_QKV_FULL), n & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(sb(s, FB_QKV_FULL), n & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         {
           uint32_t r[32], pk[16];
@@ -465,7 +471,7 @@ __global__ void __launch_bounds__(512, 1)
           mbar_arrive(sb(s, FB_KQV_READY));
         }
         // ---- softmax of S = q k^T (one row per thread, exact: S <= 128 keys)
-        if (!mbar_wait(sb(s, FB_S_FULL), n & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(sb(s, FB_S_FULL), n & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         float m8[8];   // eight independent running maxima: short dependency chains
 #pragma unroll
@@ -517,7 +523,7 @@ __global__ void __launch_bounds__(512, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_P_READY));
         // ---- ctx columns of head h = O / l, fp16, into the out-projection operand
-        if (!mbar_wait(sb(s, FB_O_FULL), n & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(sb(s, FB_O_FULL), n & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         {
           uint32_t r[32];
@@ -560,7 +566,7 @@ __global__ void __launch_bounds__(512, 1)
         mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
         tma_load_3d(xbuf, &map_x, sb(s, FB_X0), 0, 0, seq);
       }
-      if (!mbar_wait(sb(s, FB_OUT_FULL), pi & 1, abort_flag)) break;
+      if (!mbar_wait_warp(sb(s, FB_OUT_FULL), pi & 1, abort_flag)) break;
       tc_fence_after();
       if (leader) {
         for (int cc = 1; cc < NXC && cc < 3; ++cc) {
@@ -586,7 +592,7 @@ __global__ void __launch_bounds__(512, 1)
         for (int cc = 0; cc < NXC; ++cc) {
           uint64_t* bar = sb(s, FB_X0 + cc);
           const uint8_t* src = xchunk(cc);
-          if (!mbar_wait(bar, pi & 1, abort_flag)) { xok = false; break; }
+          if (!mbar_wait_warp(bar, pi & 1, abort_flag)) { xok = false; break; }
           float xv[32];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -621,9 +627,9 @@ __global__ void __launch_bounds__(512, 1)
           }
           tmem_st32(tb + 32 * cc, r);
         }
-        fence_proxy_async_smem();     // x reads before the TMA stores that reuse the buffers
-        named_bar_sync(1 + s, 128);   // all x chunks read: their buffers take y
-        if (!xok) break;
+        // Each thread reads and later overwrites only its own row of each
+        // staging buffer, so no barrier is needed between the two passes.
+        if (!__all_sync(0xffffffffu, xok)) break;
         const float dmean = (sum2.x + sum2.y) * inv_d;
         const float mean = shift + dmean;
         const float rstd = rsqrtf(fmaxf((sq2.x + sq2.y) * inv_d - dmean * dmean, 0.f) + a.eps2);
@@ -632,6 +638,8 @@ __global__ void __launch_bounds__(512, 1)
         // y leaves in 32-column fp32 atoms (16 KB, 128-byte swizzle) by TMA
         // store (rows >= S are clipped), each through the buffer its x chunk
         // came in, all in one round.
+        // Second pass: y from r (kept in TMEM by the first pass), written over
+        // this row's x in place.
         auto write_y = [&](int cc, uint8_t* ybuf) {
           uint32_t r[32];
           tmem_ld32(tb + 32 * cc, r);
@@ -651,9 +659,10 @@ __global__ void __launch_bounds__(512, 1)
         };
 #pragma unroll 1
         for (int cc = 0; cc < NXC; ++cc) write_y(cc, xchunk(cc));
-        fence_proxy_async_smem();
-        named_bar_sync(1 + s, 128);
-        if (leader) {
+        fence_proxy_async_smem();   // generic writes before the async-proxy (TMA) reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sb(s, FB_Y_STAGED));
+        if (leader && mbar_wait(sb(s, FB_Y_STAGED), pi & 1, abort_flag)) {
           if constexpr (C::WO_STAGE) {   // chunk 3 first, in its own group: it frees the weight buffer
             tma_store_3d(&map_y, wbuf, 96, 0, seq);
             bulk_commit();
