@@ -17,7 +17,10 @@ from .ref_layer import (  # noqa: F401
     TransformerConfig,
     ReferenceSelfAttention,
     ReferenceLayer,
+    ReferenceBlock,
+    ReferenceTransformer,
     build_reference_layer,
+    build_reference_transformer,
     generate_random_case,
     streamed_layer_rows_fp64,
     streamed_attention_rows_fp64,

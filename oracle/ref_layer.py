@@ -22,14 +22,15 @@ from typing import Optional, Sequence, Tuple
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 
 @dataclass(frozen=True)
 class TransformerConfig:
     """Restates ``TransformerConfig`` (torch_transformer_benchmark.py:30-57).
 
-    ``ffn_dim`` and ``num_layers`` are kept for signature compatibility; the
-    judged layer has no FFN and a single layer.
+    ``ffn_dim`` and ``num_layers`` shape the full stack (``ReferenceTransformer``);
+    the judged single layer (``ReferenceLayer``) has no FFN.
     """
 
     batch_size: int
@@ -129,6 +130,61 @@ def build_reference_layer(cfg: TransformerConfig, seed: int) -> ReferenceLayer:
     """Seeded default-init layer, as the harness builds its models (:2024, :2031)."""
     torch.manual_seed(seed)
     return ReferenceLayer(cfg.d_model, cfg.num_heads, cfg.causal).eval()
+
+
+class ReferenceBlock(nn.Module):
+    """Restates ``BaselineTransformerBlock`` (torch_transformer_benchmark.py:126-146):
+    the full pre-LN encoder block, attention half + GELU FFN half.
+
+        x1 = x + Attention(LayerNorm_1(x))                          :141
+        x2 = x1 + W2 gelu_erf(W1 LayerNorm_2(x1) + b1) + b2          :142
+        padded rows of x2 are zeroed                                 :144-145
+
+    Construction order norm1, attention, norm2, ffn_in, ffn_out (:129-133)
+    fixes the RNG draws of the seeded default init.
+    """
+
+    def __init__(self, d_model: int, num_heads: int, ffn_dim: int) -> None:
+        super().__init__()
+        self.norm1 = nn.LayerNorm(d_model)                           # :129
+        self.attention = ReferenceSelfAttention(d_model, num_heads)  # :130
+        self.norm2 = nn.LayerNorm(d_model)                           # :131
+        self.ffn_in = nn.Linear(d_model, ffn_dim)                    # :132
+        self.ffn_out = nn.Linear(ffn_dim, d_model)                   # :133
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor], causal: bool) -> torch.Tensor:
+        x = x + self.attention(self.norm1(x), valid_token_mask, causal)                    # :141
+        x = x + self.ffn_out(F.gelu(self.ffn_in(self.norm2(x)), approximate="none"))     # :142
+        if valid_token_mask is not None:                                                  # :144-145
+            x = x.masked_fill(~valid_token_mask[..., None], 0)
+        return x
+
+
+class ReferenceTransformer(nn.Module):
+    """Restates ``BaselineTransformer`` (torch_transformer_benchmark.py:149-173):
+    ``num_layers`` blocks, then ``final_norm``, padded rows zeroed.
+    ``state_dict`` keys ``layers.{i}.*`` and ``final_norm.*`` are the reference's."""
+
+    def __init__(self, config: TransformerConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.layers = nn.ModuleList([ReferenceBlock(config.d_model, config.num_heads, config.ffn_dim)
+                                     for _ in range(config.num_layers)])             # :152-160
+        self.final_norm = nn.LayerNorm(config.d_model)                                 # :161
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        for layer in self.layers:                                                      # :168-169
+            x = layer(x, valid_token_mask, self.config.causal)
+        x = self.final_norm(x)                                                         # :170
+        if valid_token_mask is not None:                                               # :171-172
+            x = x.masked_fill(~valid_token_mask[..., None], 0)
+        return x
+
+
+def build_reference_transformer(cfg: TransformerConfig, seed: int) -> ReferenceTransformer:
+    """Seeded default-init stack, as the harness builds its baseline (:2024-2031)."""
+    torch.manual_seed(seed)
+    return ReferenceTransformer(cfg).eval()
 
 
 def generate_random_case(cfg: TransformerConfig, seed: int, padding_ratio: float = 0.0,

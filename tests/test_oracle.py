@@ -5,12 +5,14 @@ import hashlib
 import pytest
 import torch
 
-from oracle import (ReferenceLayer, TransformerConfig, build_reference_layer, compare_outputs,
-                    generate_random_case, streamed_attention_rows_fp64, streamed_layer_rows_fp64)
+from oracle import (ReferenceLayer, TransformerConfig, build_reference_layer, build_reference_transformer,
+                    compare_outputs, generate_random_case, streamed_attention_rows_fp64,
+                    streamed_layer_rows_fp64)
 from oracle.ref_layer import sample_rows
 from tests.conftest import GOLDEN
 
-FIXTURES = sorted(p.name for p in GOLDEN.glob("*.pt"))
+FIXTURES = sorted(p.name for p in GOLDEN.glob("*.pt") if not p.name.startswith("model_"))
+MODEL_FIXTURES = sorted(p.name for p in GOLDEN.glob("model_*.pt"))
 
 
 def _sha(sd):
@@ -23,6 +25,26 @@ def _sha(sd):
 
 def test_fixtures_present():
     assert len(FIXTURES) >= 8
+    assert len(MODEL_FIXTURES) >= 4
+
+
+@pytest.mark.parametrize("name", MODEL_FIXTURES)
+def test_stack_oracle_bit_exact_vs_reference_fixture(name):
+    """Full stacks (blocks with the GELU FFN, final_norm) produced by the
+    reference's own BaselineTransformer (tests/golden/make_golden.py)."""
+    g = torch.load(GOLDEN / name)
+    cfg = TransformerConfig(g["B"], g["S"], g["d"], g["H"], ffn_dim=g["ffn_dim"],
+                            num_layers=g["num_layers"], causal=g["causal"])
+    model = build_reference_transformer(cfg, g["weight_seed"])
+    assert _sha(model.state_dict()) == g["state_sha"]
+    if "state_dict" in g:
+        model.load_state_dict(g["state_dict"], strict=True)
+    for t in g["trials"]:
+        x_again, _ = generate_random_case(cfg, t["seed"], g["padding"])
+        assert torch.equal(x_again, t["x"])
+        with torch.inference_mode():
+            y = model(t["x"], t["mask"])
+        assert torch.equal(y, t["y"]), f"{name}: stack oracle differs from the reference output"
 
 
 @pytest.mark.parametrize("name", FIXTURES)
