@@ -17,7 +17,8 @@ EXPORTED = (
     "b200l_version", "b200l_last_error", "b200l_layer_workspace_bytes",
     "b200l_clear_status", "b200l_read_status", "b200l_pack_weights",
     "b200l_layer_forward", "b200l_qkv_ln_gemm", "b200l_flash_attn",
-    "b200l_outproj_res_ln", "b200l_layer_forward_noalloc",
+    "b200l_outproj_res_ln", "b200l_layer_forward_noalloc", "b200l_block_workspace_bytes",
+    "b200l_block_forward", "b200l_row_layernorm", "b200l_cast_f16",
 )
 
 ABI_VERSION = 2
@@ -49,6 +50,15 @@ class LayerDesc(ctypes.Structure):
     ]
 
 
+class BlockDesc(ctypes.Structure):
+    """Mirror of ``b200l_block_desc``."""
+
+    _fields_ = [
+        ("layer", LayerDesc), ("ffn_dim", c_int32),
+        ("w1", c_void_p), ("b1", c_void_p), ("w2", c_void_p), ("b2", c_void_p),
+    ]
+
+
 class B200LError(RuntimeError):
     """A C-ABI call returned a negative status."""
 
@@ -75,6 +85,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         "b200l_flash_attn": (c_int, [P, P, c_size_t, P]),
         "b200l_outproj_res_ln": (c_int, [P, P, P, P, c_size_t, P]),
         "b200l_layer_forward_noalloc": (c_int, [P, P, P, P]),
+        "b200l_block_workspace_bytes": (c_size_t, [P]),
+        "b200l_block_forward": (c_int, [P, P, P, P, c_size_t, P]),
+        "b200l_row_layernorm": (c_int, [P, P, P, P, c_float, ctypes.c_int64, c_int32, P, P]),
+        "b200l_cast_f16": (c_int, [P, P, ctypes.c_int64, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

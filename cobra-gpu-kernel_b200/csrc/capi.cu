@@ -213,20 +213,20 @@ int check_launch(const char* what) {
 // ---------------------------------------------------------------- launches
 template <int VPL, bool F16>
 int launch_row_ln_t(const float* in, void* out, const float* w, const float* b, float eps, long long T, int d,
-                    cudaStream_t st) {
+                    cudaStream_t st, const uint8_t* rowmask) {
   const long long blocks = (T + 7) / 8;
-  row_ln_kernel<VPL, F16><<<(unsigned)blocks, 256, 0, st>>>(in, out, w, b, eps, T, d);
+  row_ln_kernel<VPL, F16><<<(unsigned)blocks, 256, 0, st>>>(in, out, w, b, eps, T, d, rowmask);
   return check_launch("row_ln_kernel");
 }
 template <bool F16>
 int launch_row_ln(const float* in, void* out, const float* w, const float* b, float eps, long long T, int d,
-                  cudaStream_t st) {
+                  cudaStream_t st, const uint8_t* rowmask = nullptr) {
   const int v = (d + 127) / 128;
-  if (v <= 1) return launch_row_ln_t<1, F16>(in, out, w, b, eps, T, d, st);
-  if (v <= 2) return launch_row_ln_t<2, F16>(in, out, w, b, eps, T, d, st);
-  if (v <= 4) return launch_row_ln_t<4, F16>(in, out, w, b, eps, T, d, st);
-  if (v <= 8) return launch_row_ln_t<8, F16>(in, out, w, b, eps, T, d, st);
-  return launch_row_ln_t<16, F16>(in, out, w, b, eps, T, d, st);
+  if (v <= 1) return launch_row_ln_t<1, F16>(in, out, w, b, eps, T, d, st, rowmask);
+  if (v <= 2) return launch_row_ln_t<2, F16>(in, out, w, b, eps, T, d, st, rowmask);
+  if (v <= 4) return launch_row_ln_t<4, F16>(in, out, w, b, eps, T, d, st, rowmask);
+  if (v <= 8) return launch_row_ln_t<8, F16>(in, out, w, b, eps, T, d, st, rowmask);
+  return launch_row_ln_t<16, F16>(in, out, w, b, eps, T, d, st, rowmask);
 }
 
 template <int KP>
@@ -368,7 +368,7 @@ int run_outproj(const b200l_layer_desc* desc, const Plan& p, const float* x, flo
   }
   if ((rc = map_rows_k(&map_b, desc->wo, (unsigned long long)p.d, p.d, 256, "wo"))) return rc;
   if ((rc = launch_gemm_tma_t<256, 4, EPI_RESID>(map_a, map_b, ea, p.T, p.d, p.d, ws, st))) return rc;
-  return launch_row_ln<false>(y, y, desc->ln2_w, desc->ln2_b, desc->eps2, p.T, p.d, st);
+  return launch_row_ln<false>(y, y, desc->ln2_w, desc->ln2_b, desc->eps2, p.T, p.d, st, nullptr);
 }
 
 // Whole-layer kernel for d_model in {64, 128}, head_dim 32, S <= 128.
@@ -416,6 +416,89 @@ int run_fused(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, c
               cudaStream_t st) {
   if (p.d == 128) return launch_fused_t<128>(desc, p, dev, x, y, ws, st);
   return launch_fused_t<64>(desc, p, dev, x, y, ws, st);
+}
+
+// ------------------------------------------------------------------ full block
+// x1 = x + Attn(LN1(x)); x2 = x1 + W2 gelu(W1 LN2(x1) + b1) + b2, padded rows
+// of x2 zeroed -- BaselineTransformerBlock.forward (torch_transformer_benchmark.py
+// :141-145), computed as the reference's fused path does (:1274-1292): the
+// out-projection keeps the fp32 residual x1, a row pass writes LN2(x1) in
+// fp16, the FFN-in GEMM applies bias + exact GELU in its epilogue and the
+// FFN-out GEMM adds bias and residual and zeroes padded rows in its.
+struct BlockPlan {
+  Plan p;
+  int f;
+  size_t off_x1, off_h2, off_h1, total;
+};
+
+int make_block_plan(const b200l_block_desc* bd, BlockPlan* bp) {
+  if (!bd) return fail(B200L_ERR_NULL_POINTER, "block descriptor is NULL");
+  int rc = make_plan(&bd->layer, &bp->p);
+  if (rc) return rc;
+  const int f = bd->ffn_dim;
+  if (f <= 0 || f % 8 != 0 || f > 65536)
+    return fail(B200L_ERR_BAD_SHAPE, "ffn_dim %d unsupported: need a positive multiple of 8, at most 65536", f);
+  bp->f = f;
+  const Plan& p = bp->p;
+  size_t off = align_up(p.total, 1024);
+  bp->off_x1 = off; off = align_up(off + (size_t)p.T * p.d * 4, 1024);
+  bp->off_h2 = off; off = align_up(off + (size_t)p.T * p.d * 2, 1024);
+  bp->off_h1 = off; off = align_up(off + (size_t)p.T * f * 2, 1024);
+  bp->total = off;
+  return B200L_OK;
+}
+
+// y = x + acc + bias over a [T, d] output with K-major fp16 operands (A [T, K],
+// B [d, K]); rowmask_zero selects the padded-row rule (keep x / zero the row).
+int run_resid_gemm(const void* a, int K, const void* bmat, int d, const float* bias, const float* x, float* y,
+                   const uint8_t* rowmask, int rowmask_zero, long long T, void* ws, cudaStream_t st) {
+  EpiArgs ea{};
+  ea.bias = bias;
+  ea.x = x;
+  ea.y = y;
+  ea.d = d;
+  ea.rowmask = rowmask;
+  ea.rowmask_zero = rowmask_zero;
+  CUtensorMap map_a, map_b;
+  int rc = map_rows_k(&map_a, a, (unsigned long long)T, K, 128, "gemm A");
+  if (rc) return rc;
+  const int bn = d <= 256 ? (d + 63) / 64 * 64 : 256;
+  if ((rc = map_rows_k(&map_b, bmat, (unsigned long long)d, K, (unsigned)bn, "gemm B"))) return rc;
+  switch (bn) {
+    case 64: return launch_gemm_tma_t<64, 2, EPI_RESID>(map_a, map_b, ea, T, K, d, ws, st);
+    case 128: return launch_gemm_tma_t<128, 2, EPI_RESID>(map_a, map_b, ea, T, K, d, ws, st);
+    case 192: return launch_gemm_tma_t<192, 3, EPI_RESID>(map_a, map_b, ea, T, K, d, ws, st);
+    default: return launch_gemm_tma_t<256, 4, EPI_RESID>(map_a, map_b, ea, T, K, d, ws, st);
+  }
+}
+
+int run_block(const b200l_block_desc* bd, const BlockPlan& bp, const DevInfo& dev, const float* x, float* y,
+              void* ws, cudaStream_t st) {
+  const b200l_layer_desc* desc = &bd->layer;
+  const Plan& p = bp.p;
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  float* x1 = reinterpret_cast<float*>(w + bp.off_x1);
+  __half* h2 = reinterpret_cast<__half*>(w + bp.off_h2);
+  __half* h1 = reinterpret_cast<__half*>(w + bp.off_h1);
+  int rc;
+  if ((rc = run_qkv(desc, p, x, ws, st))) return rc;
+  if ((rc = run_attn(desc, p, dev, ws, st))) return rc;
+  // x1 = x + (valid row ? ctx Wo^T + bo : 0)
+  if ((rc = run_resid_gemm(w + p.off_ctx, p.d, desc->wo, p.d, desc->bo, x, x1, desc->valid_mask, 0, p.T, ws, st)))
+    return rc;
+  if ((rc = launch_row_ln<true>(x1, h2, desc->ln2_w, desc->ln2_b, desc->eps2, p.T, p.d, st))) return rc;
+  {  // h1 = fp16(gelu(h2 W1^T + b1))
+    EpiArgs ea{};
+    ea.bias = bd->b1;
+    ea.h = h1;
+    ea.ldh = bp.f;
+    CUtensorMap map_a, map_b;
+    if ((rc = map_rows_k(&map_a, h2, (unsigned long long)p.T, p.d, 128, "LN2 output"))) return rc;
+    if ((rc = map_rows_k(&map_b, bd->w1, (unsigned long long)bp.f, p.d, 256, "ffn_in weight"))) return rc;
+    if ((rc = launch_gemm_tma_t<256, 4, EPI_GELU>(map_a, map_b, ea, p.T, p.d, bp.f, ws, st))) return rc;
+  }
+  // y = valid row ? x1 + h1 W2^T + b2 : 0
+  return run_resid_gemm(h1, bp.f, bd->w2, p.d, bd->b2, x1, y, desc->valid_mask, 1, p.T, ws, st);
 }
 
 int check_xy(const void* x, const void* y, bool need_y) {
@@ -522,6 +605,52 @@ int b200l_layer_forward(const b200l_layer_desc* desc, const float* x, float* y, 
   if ((rc = run_qkv(desc, p, x, workspace, st))) return rc;
   if ((rc = run_attn(desc, p, dev, workspace, st))) return rc;
   return run_outproj(desc, p, x, y, workspace, st);
+}
+
+size_t b200l_block_workspace_bytes(const b200l_block_desc* desc) {
+  BlockPlan bp;
+  if (make_block_plan(desc, &bp)) return 0;
+  return bp.total;
+}
+
+int b200l_block_forward(const b200l_block_desc* desc, const float* x, float* y, void* workspace, size_t ws_bytes,
+                        void* stream) {
+  BlockPlan bp;
+  int rc = make_block_plan(desc, &bp);
+  if (rc) return rc;
+  if (!desc->w1 || !desc->b1 || !desc->w2 || !desc->b2) return fail(B200L_ERR_NULL_POINTER, "FFN weight is NULL");
+  Plan p;
+  DevInfo dev;
+  if ((rc = check_common(&desc->layer, workspace, ws_bytes, &p, &dev))) return rc;
+  if (ws_bytes < bp.total)
+    return fail(B200L_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < %zu needed", ws_bytes, bp.total);
+  if ((rc = check_xy(x, y, true))) return rc;
+  return run_block(desc, bp, dev, x, y, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int b200l_row_layernorm(const float* x, float* y, const float* w, const float* b, float eps, int64_t rows,
+                        int32_t d, const uint8_t* row_mask, void* stream) {
+  if (!x || !y || !w || !b) return fail(B200L_ERR_NULL_POINTER, "row_layernorm: NULL pointer");
+  if (rows <= 0 || d <= 0 || d % 4 != 0 || d > 2048)
+    return fail(B200L_ERR_BAD_SHAPE, "row_layernorm: rows %lld, d %d (need d a multiple of 4 in [4, 2048])",
+                (long long)rows, d);
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16)
+    return fail(B200L_ERR_ALIGNMENT, "row_layernorm: x and y must be 16-byte aligned");
+  DevInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  return launch_row_ln<false>(x, y, w, b, eps, rows, d, static_cast<cudaStream_t>(stream), row_mask);
+}
+
+int b200l_cast_f16(const float* src, void* dst, int64_t n, void* stream) {
+  if (!src || !dst) return fail(B200L_ERR_NULL_POINTER, "cast_f16: NULL pointer");
+  if (n <= 0) return fail(B200L_ERR_BAD_SHAPE, "cast_f16: n must be positive");
+  DevInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  const long long blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
+  cast_f16_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(src, static_cast<__half*>(dst), n);
+  return check_launch("cast_f16_kernel");
 }
 
 }  // extern "C"

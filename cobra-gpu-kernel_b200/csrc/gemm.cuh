@@ -264,11 +264,12 @@ __global__ void __launch_bounds__(256, 1)
 //   EPI_QKV       bias + scatter into q / k / v^T        (QKV for d > 256)
 //   EPI_RESID     y = x + acc + bias  (fp32, pre-LN)      (out-proj for d > 256)
 //   EPI_RESID_LN  y = LN2(x + acc + bias), BN >= d        (out-proj for d <= 256)
+//   EPI_GELU      h = fp16(gelu_erf(acc + bias))          (FFN in, :142, :326-328)
 // The residual is added to the fp32 accumulator and never rounded to fp16
 // before the add (the reference's fp32-store rule, :187-191, :350-353).
 // Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-5 epilogue.
 // ===========================================================================
-enum EpiKind : int { EPI_QKV = 0, EPI_RESID = 1, EPI_RESID_LN = 2 };
+enum EpiKind : int { EPI_QKV = 0, EPI_RESID = 1, EPI_RESID_LN = 2, EPI_GELU = 3 };
 
 struct EpiArgs {
   QkvOut qkv;
@@ -280,6 +281,9 @@ struct EpiArgs {
   float eps;
   int d;
   const uint8_t* rowmask;  // EPI_RESID*: token validity uint8 [T] or nullptr; invalid rows get y = x (+ LN)
+  int rowmask_zero;        // EPI_RESID: invalid rows get y = 0 instead (end of a block, :144-145)
+  __half* h;               // EPI_GELU output, fp16 [T, ldh]
+  int ldh;
 };
 
 template <int BN, int ST>
@@ -392,18 +396,47 @@ __global__ void __launch_bounds__(192, 1)
             const float* xr = ea.x + t * ea.d + col0;
             float* yr = ea.y + t * ea.d + col0;
             // A padded query row's attention output is zeroed (bias included):
-            // y = x there (BaselineSelfAttention, :121-122).
+            // y = x there (BaselineSelfAttention, :121-122); at the end of a
+            // block the whole padded row is zeroed instead (:144-145).
             const bool keep = ea.rowmask == nullptr || ea.rowmask[t] != 0;
+            const float xs = (!keep && ea.rowmask_zero) ? 0.f : 1.f;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               const float4 xv = __ldg(reinterpret_cast<const float4*>(xr) + c);
               const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.bias + col0) + c);
               float4 o;
-              o.x = xv.x + (keep ? __uint_as_float(r[4 * c + 0]) + bv.x : 0.f);
-              o.y = xv.y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
-              o.z = xv.z + (keep ? __uint_as_float(r[4 * c + 2]) + bv.z : 0.f);
-              o.w = xv.w + (keep ? __uint_as_float(r[4 * c + 3]) + bv.w : 0.f);
+              o.x = xs * xv.x + (keep ? __uint_as_float(r[4 * c + 0]) + bv.x : 0.f);
+              o.y = xs * xv.y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
+              o.z = xs * xv.z + (keep ? __uint_as_float(r[4 * c + 2]) + bv.z : 0.f);
+              o.w = xs * xv.w + (keep ? __uint_as_float(r[4 * c + 3]) + bv.w : 0.f);
               reinterpret_cast<float4*>(yr)[c] = o;
+            }
+          }
+        }
+      } else if constexpr (EPI == EPI_GELU) {
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          const int col0 = n0 + cc * 32;
+          if (col0 >= N) break;
+          uint32_t r[32];
+          tmem_ld32(tl + cc * 32, r);
+          if (valid) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {   // 8 columns -> one 16-byte store
+              const int c0 = col0 + 8 * g;
+              if (c0 < N) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float v0 = __uint_as_float(r[8 * g + 2 * e]) + __ldg(ea.bias + c0 + 2 * e);
+                  float v1 = __uint_as_float(r[8 * g + 2 * e + 1]) + __ldg(ea.bias + c0 + 2 * e + 1);
+                  // exact GELU, F.gelu(approximate="none"): 0.5 v (1 + erf(v / sqrt(2)))
+                  v0 = 0.5f * v0 * (1.0f + erff(v0 * 0.70710678118654752f));
+                  v1 = 0.5f * v1 * (1.0f + erff(v1 * 0.70710678118654752f));
+                  w[e] = pack_half2(v0, v1);
+                }
+                *reinterpret_cast<uint4*>(ea.h + t * ea.ldh + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+              }
             }
           }
         }

@@ -5,8 +5,10 @@
 // biased variance over the row, y = (x - mean) * rsqrt(var + eps) * w + b,
 // statistics in fp32. One warp per row, coalesced float4 traffic, the row kept
 // in registers between the mean and variance passes (two-pass variance).
-// These passes are used only where the GEMM epilogue cannot see a whole row
-// (d_model > 256); for d_model <= 256 the LayerNorms live inside K1 and K3.
+// These passes are used where a GEMM epilogue cannot see a whole row
+// (d_model > 256), for the block's LN2 (whose fp32 input, the residual, is
+// kept for the FFN) and for the stack's final_norm; a row mask zeroes padded
+// rows of the output (:170-172).
 #pragma once
 
 #include "common.cuh"
@@ -17,11 +19,13 @@ namespace b200l {
 template <int VPL, bool OUT_F16>
 __global__ void __launch_bounds__(256) row_ln_kernel(const float* __restrict__ in, void* __restrict__ out,
                                                      const float* __restrict__ w, const float* __restrict__ b,
-                                                     float eps, long long T, int d) {
+                                                     float eps, long long T, int d,
+                                                     const uint8_t* __restrict__ rowmask) {
   const int warps = blockDim.x >> 5;
   const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
+  const bool zero = rowmask != nullptr && rowmask[row] == 0;
   const float* src = in + row * d;
   float4 v[VPL];
   float s = 0.f;
@@ -58,6 +62,7 @@ __global__ void __launch_bounds__(256) row_ln_kernel(const float* __restrict__ i
       y.y = (v[i].y - mean) * rstd * ww.y + bb.y;
       y.z = (v[i].z - mean) * rstd * ww.z + bb.z;
       y.w = (v[i].w - mean) * rstd * ww.w + bb.w;
+      if (zero) y = make_float4(0.f, 0.f, 0.f, 0.f);
       if constexpr (OUT_F16) {
         uint2 p;
         p.x = pack_half2(y.x, y.y);
@@ -94,6 +99,12 @@ __global__ void pack_weights_kernel(int d, const float* __restrict__ wq, const f
       bqkv32[i] = bsrc[i - (long long)w2 * d];
     }
   }
+}
+
+// dst[i] = fp16(src[i]): weight packing for the FFN matrices.
+__global__ void cast_f16_kernel(const float* __restrict__ src, __half* __restrict__ dst, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    dst[i] = __float2half_rn(src[i]);
 }
 
 }  // namespace b200l

@@ -145,6 +145,42 @@ B200L_API int b200l_flash_attn(const b200l_layer_desc* desc, void* workspace, si
 B200L_API int b200l_outproj_res_ln(const b200l_layer_desc* desc, const float* x, float* y,
                          void* workspace, size_t ws_bytes, void* stream);
 
+/* Full encoder block, for stacks that include the reference's GELU FFN:
+ *   x1 = x + Attn(LN1(x)); y = x1 + W2 gelu_erf(W1 LN2(x1) + b1) + b2,
+ * padded rows of y zeroed (valid_mask). The attention half uses the layer
+ * kernels; the FFN half is two tcgen05 GEMMs (bias + exact GELU to fp16 in the
+ * first epilogue, bias + residual + row mask in the second).
+ * Replaces BaselineTransformerBlock.forward (torch_transformer_benchmark.py:
+ * 135-146) as the reference's fused path computes it (:1274-1292: _tl_linear
+ * with resid, _tl_add_ln, _tl_linear gelu=True, _tl_linear with rmask). */
+typedef struct b200l_block_desc {
+    b200l_layer_desc layer;  /* attention half, norm1, norm2 (eps2 is norm2's) */
+    int32_t ffn_dim;         /* f, a positive multiple of 8 */
+    const void* w1;          /* fp16 [f, d]  ffn_in.weight */
+    const float* b1;         /* fp32 [f]     ffn_in.bias */
+    const void* w2;          /* fp16 [d, f]  ffn_out.weight */
+    const float* b2;         /* fp32 [d]     ffn_out.bias */
+} b200l_block_desc;
+
+/* Workspace bytes of b200l_block_forward: the layer workspace, then the fp32
+ * residual x1 [T, d], LN2(x1) fp16 [T, d] and the FFN hidden fp16 [T, f]. */
+B200L_API size_t b200l_block_workspace_bytes(const b200l_block_desc* desc);
+
+B200L_API int b200l_block_forward(const b200l_block_desc* desc, const float* x, float* y,
+                                  void* workspace, size_t ws_bytes, void* stream);
+
+/* y = LayerNorm(x) row by row (fp32 in/out, d a multiple of 4, at most 2048),
+ * rows whose row_mask byte is 0 set to zero (row_mask may be NULL). x may equal
+ * y. The stack's final_norm and its padded-row mask: replaces
+ * BaselineTransformer.forward :170-172 (fused as _tl_add_ln mask_out, :1289-1291). */
+B200L_API int b200l_row_layernorm(const float* x, float* y, const float* w, const float* b, float eps,
+                                  int64_t rows, int32_t d, const uint8_t* row_mask, void* stream);
+
+/* dst = fp16(src) for n elements: packs nn.Linear weights for the FFN GEMMs.
+ * Replaces the fp16 weight copies of _LayerPack (torch_transformer_benchmark.py:
+ * 873-914) for ffn_in / ffn_out. */
+B200L_API int b200l_cast_f16(const float* src, void* dst, int64_t n, void* stream);
+
 /* Allocation-free variant of b200l_layer_forward. No counterpart in the
  * reference (its Python module always allocates through PyTorch).
  *

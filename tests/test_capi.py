@@ -75,21 +75,22 @@ def test_no_cpu_fallback(pkg):
         layer(torch.zeros(1, 4, 128))
 
 
-def test_descriptor_layout_matches_header(pkg, tmp_path):
-    """The ctypes mirror of b200l_layer_desc has the C struct's size and field
-    offsets (compiled from include/cobra_b200.h with the host C compiler)."""
+@pytest.mark.parametrize("struct,cls", [("b200l_layer_desc", "LayerDesc"), ("b200l_block_desc", "BlockDesc")])
+def test_descriptor_layout_matches_header(pkg, tmp_path, struct, cls):
+    """The ctypes mirrors of the descriptors have the C structs' sizes and
+    field offsets (compiled from include/cobra_b200.h with the host C compiler)."""
     import shutil
     import subprocess
     cc = shutil.which("gcc") or shutil.which("cc")
     if cc is None:
         pytest.skip("no host C compiler")
-    D = pkg._lib.LayerDesc
+    D = getattr(pkg._lib, cls)
     names = [f[0] for f in D._fields_]
     src = tmp_path / "layout.c"
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "cobra_b200.h"\nint main(void) {\n'
-        '  printf("%zu\\n", sizeof(b200l_layer_desc));\n'
-        + "".join(f'  printf("%zu\\n", offsetof(b200l_layer_desc, {n}));\n' for n in names)
+        f'  printf("%zu\\n", sizeof({struct}));\n'
+        + "".join(f'  printf("%zu\\n", offsetof({struct}, {n}));\n' for n in names)
         + "  return 0;\n}\n")
     exe = tmp_path / "layout"
     subprocess.run([cc, "-I", str(ROOT / "include"), "-o", str(exe), str(src)], check=True)

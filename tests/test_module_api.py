@@ -53,3 +53,30 @@ def test_module_built_under_inference_mode_tracks_parameters(pkg):
     with torch.inference_mode():
         lay.norm1.weight = torch.nn.Parameter(torch.ones(64))
     assert lay._param_versions() != v1
+
+
+def test_stack_state_dict_and_seeded_init_match_reference(pkg):
+    """B200Transformer has the reference BaselineTransformer's module tree:
+    identical state_dict keys, and seeded construction draws identical weights
+    (the harness copies baseline weights with strict=True, :1544-1554)."""
+    import torch
+    from oracle import TransformerConfig as OCfg, build_reference_transformer
+    ocfg = OCfg(2, 16, 64, 2, ffn_dim=96, num_layers=3, causal=True)
+    ref = build_reference_transformer(ocfg, seed=5)
+    cfg = pkg.TransformerConfig(2, 16, 64, 2, ffn_dim=96, num_layers=3, causal=True)
+    torch.manual_seed(5)
+    ours = pkg.B200Transformer(cfg)
+    rs, os_ = ref.state_dict(), ours.state_dict()
+    assert list(rs) == list(os_)
+    assert all(torch.equal(rs[k], os_[k]) for k in rs)
+    ours.load_state_dict(rs, strict=True)
+    assert pkg.UserOptimizedTransformer is pkg.B200Transformer
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        ours(torch.zeros(2, 16, 64))
+
+
+def test_stack_config_validation(pkg):
+    with pytest.raises(ValueError, match="ffn_dim"):
+        pkg.B200Transformer(pkg.TransformerConfig(1, 8, 64, 2, ffn_dim=0, num_layers=1))
+    with pytest.raises(ValueError, match="num_layers"):
+        pkg.B200Transformer(pkg.TransformerConfig(1, 8, 64, 2, ffn_dim=64, num_layers=0))
