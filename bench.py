@@ -222,6 +222,64 @@ def run_reference_arm(args, cfg):
     return 0
 
 
+def run_stack(args, cfg) -> int:
+    """Full stack (blocks with the GELU FFN + final_norm) on one GPU: device-
+    resident x, CUDA events around each forward, inputs larger than L2 or the
+    L2 flushed between steps."""
+    import __graft_entry__
+    from oracle import TransformerConfig as OCfg, build_reference_transformer
+
+    pkg = __graft_entry__.load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, S, d, H = cfg["B"], cfg["S"], cfg["d"], cfg["H"]
+    f = args.ffn or 4 * d
+    L = args.layers
+    ocfg = OCfg(B, S, d, H, ffn_dim=f, num_layers=L)
+    ref = build_reference_transformer(ocfg, 1234)
+    model = pkg.B200Transformer(pkg.TransformerConfig(B, S, d, H, ffn_dim=f, num_layers=L)).to(dev).eval()
+    model.load_state_dict(ref.state_dict(), strict=True)
+    g = torch.Generator(device="cpu").manual_seed(1234 + 100000)
+    x = torch.randn(B, S, d, generator=g).to(dev)
+    big = x.numel() * 4 > L2_BYTES
+    flush = None if big else torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            model(x)
+        torch.cuda.synchronize(dev)
+        model.check_status()
+        times = []
+        for _ in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            model(x)
+            e1.record()
+            times.append((e0, e1))
+        torch.cuda.synchronize(dev)
+        model.check_status()
+    ms = statistics.fmean(a.elapsed_time(b) for a, b in times)
+    T = B * S
+    flops = L * (8.0 * T * d * d + 4.0 * B * S * S * d + 4.0 * T * d * f)
+    pk_ = peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    launches = L * (6 + (1 if d > 256 else 0)) + 1
+    print(json.dumps({
+        "metric": "stack tokens/s (B*S/latency)", "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate, fp32 in/out",
+        "data": "synthetic: x ~ N(0,1) fp32, seeded default init of the reference's BaselineTransformer",
+        "config": {"workload": f"{args.config} shape, {L} blocks, ffn_dim {f}", **cfg, "layers": L, "ffn_dim": f,
+                   "l2": "inputs larger than L2" if big else "L2 flushed between steps"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk_["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / pk_["bf16_tflops"], "kernel": "whole forward (all GEMMs + attention)",
+                     "traffic": None, "peak_source": pk_["source"]},
+        "gpu_launches": launches * args.steps,
+    }))
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -234,6 +292,10 @@ def main() -> int:
                     help="pieces per rank for the scatter/gather measurement (N > 1)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (smaller cases for ncu captures)")
+    ap.add_argument("--model", default="layer", choices=["layer", "stack"],
+                    help="layer: the judged single layer (default); stack: full blocks with the GELU FFN")
+    ap.add_argument("--layers", type=int, default=2, help="--model stack: number of blocks")
+    ap.add_argument("--ffn", type=int, default=0, help="--model stack: ffn_dim (default 4*d)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = dict(CONFIGS[args.config])
@@ -242,6 +304,8 @@ def main() -> int:
 
     if args.impl == "reference":
         return run_reference_arm(args, cfg)
+    if args.model == "stack":
+        return run_stack(args, cfg)
 
     import ctypes
     import datetime
