@@ -250,9 +250,11 @@ int launch_gemm_tma_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
   const int smem = GemmTmaCfg<BN, ST>::SMEM;
   int rc = ensure_smem((const void*)kern, smem);
   if (rc) return rc;
-  const long long blocks = ((T + 127) / 128) * ((N + BN - 1) / BN);
-  if (blocks > 0x7fffffffLL) return fail(B200L_ERR_BAD_SHAPE, "grid too large");
-  kern<<<(unsigned)blocks, 192, smem, st>>>(map_a, map_b, ea, T, K, N, reinterpret_cast<DevStatus*>(ws));
+  DevInfo dev;
+  if ((rc = device_info(&dev))) return rc;
+  const long long tiles = ((T + 127) / 128) * ((N + BN - 1) / BN);   // persistent: at most one CTA per SM
+  const unsigned grid = (unsigned)(tiles < dev.sms ? tiles : dev.sms);
+  kern<<<grid, 192, smem, st>>>(map_a, map_b, ea, T, K, N, reinterpret_cast<DevStatus*>(ws));
   return check_launch("gemm_tma_kernel");
 }
 

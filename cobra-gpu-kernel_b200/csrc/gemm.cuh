@@ -259,7 +259,10 @@ __global__ void __launch_bounds__(256, 1)
 
 // ===========================================================================
 // TMA-fed GEMM: D[128 x BN] = A[128 x K] * B[BN x K]^T over a ST-stage ring of
-// (A 128x64, B BNx64) fp16 tiles, one accumulator of BN TMEM columns.
+// (A 128x64, B BNx64) fp16 tiles. Persistent: each CTA walks output tiles
+// (m-major, so neighbouring tiles share A), the producer and the MMA issuer
+// run ahead across tile boundaries, and two TMEM accumulators (when 2*BN fits
+// in 512 columns) let the epilogue of one tile overlap the MMAs of the next.
 // Epilogues:
 //   EPI_QKV       bias + scatter into q / k / v^T        (QKV for d > 256)
 //   EPI_RESID     y = x + acc + bias  (fp32, pre-LN)      (out-proj for d > 256)
@@ -292,7 +295,9 @@ struct GemmTmaCfg {
   static constexpr int B_BYTES = BN * 128;   // BN rows x 64 fp16
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int SMEM = ST * STAGE + 256 + 1024;
-  static constexpr int TMEM_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+  static constexpr int ACC_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+  static constexpr int NACC = 2 * ACC_COLS <= 512 ? 2 : 1;      // TMEM accumulators
+  static constexpr int TMEM_COLS = NACC * ACC_COLS;
 };
 
 template <int BN, int ST, int EPI>
@@ -303,16 +308,17 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST * C::STAGE);
-  uint64_t* full = bars;             // [ST]
-  uint64_t* empty = bars + ST;       // [ST]
-  uint64_t* acc_full = bars + 2 * ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * ST + 2);
+  uint64_t* full = bars;                    // [ST]
+  uint64_t* empty = bars + ST;              // [ST]
+  uint64_t* acc_full = bars + 2 * ST;       // [NACC]
+  uint64_t* acc_empty = bars + 2 * ST + 2;  // [NACC], one arrival per epilogue warp
+  uint64_t* mma_done = bars + 2 * ST + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * ST + 6);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NT = (N + BN - 1) / BN;
-  const long long m0 = (long long)(blockIdx.x / NT) * 128;
-  const int n0 = (blockIdx.x % NT) * BN;
+  const long long tiles = ((T + 127) / 128) * NT;
   const int KT = (K + 63) / 64;
 
   if (threadIdx.x == 0) {
@@ -320,7 +326,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&map_a);
@@ -335,46 +345,68 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {  // ---- producer
+    if (lane == 0) {  // ---- producer: A/B k-tiles of every tile of this CTA, in order
       int last[ST];
       for (int i = 0; i < ST; ++i) last[i] = -1;
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % ST;
-        if (!mbar_wait(&empty[s], ((kt / ST) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&full[s], C::STAGE);
-        uint8_t* st = smem + s * C::STAGE;
-        tma_load_2d(st, &map_a, &full[s], kt * 64, (int)m0);
-        tma_load_2d(st + C::A_BYTES, &map_b, &full[s], kt * 64, n0);
-        last[s] = kt;
+      long long it = 0;
+      bool ok = true;
+      for (long long tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const long long m0 = (tile / NT) * 128;
+        const int n0 = (int)(tile % NT) * BN;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = (int)(it % ST);
+          if (!mbar_wait(&empty[s], (uint32_t)((it / ST) & 1) ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], C::STAGE);
+          uint8_t* st = smem + s * C::STAGE;
+          tma_load_2d(st, &map_a, &full[s], kt * 64, (int)m0);
+          tma_load_2d(st + C::A_BYTES, &map_b, &full[s], kt * 64, n0);
+          last[s] = (int)(it / ST);
+        }
       }
       for (int s = 0; s < ST; ++s)
-        if (last[s] >= 0) mbar_drain(&full[s], (last[s] / ST) & 1);
+        if (last[s] >= 0) mbar_drain(&full[s], last[s] & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer
       const uint32_t idesc = idesc_f16_f32(128, BN);
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % ST;
-        if (!mbar_wait(&full[s], (kt / ST) & 1, abort_flag)) break;
+      long long it = 0;
+      int ti = 0;
+      bool ok = true;
+      for (long long tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+        const int a = ti % C::NACC;
+        const int use = ti / C::NACC;   // earlier tiles that used accumulator a
+        if (use > 0 && !mbar_wait(&acc_empty[a], (use - 1) & 1, abort_flag)) break;
         tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + s * C::STAGE);
-        const uint32_t b_base = a_base + C::A_BYTES;
+        const uint32_t d_tmem = tmem_base + a * C::ACC_COLS;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = (int)(it % ST);
+          if (!mbar_wait(&full[s], (uint32_t)((it / ST) & 1), abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + s * C::STAGE);
+          const uint32_t b_base = a_base + C::A_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16_ss(tmem_base, sdesc_kmajor(a_base + kk * 32, 128), sdesc_kmajor(b_base + kk * 32, 128), idesc,
-                      (kt | kk) ? 1u : 0u);
-        umma_commit(&empty[s]);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_ss(d_tmem, sdesc_kmajor(a_base + kk * 32, 128), sdesc_kmajor(b_base + kk * 32, 128), idesc,
+                        (kt | kk) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[a]);
       }
-      umma_commit(acc_full);
-      mbar_drain(acc_full, 0);
+      umma_commit(mma_done);
+      mbar_drain(mma_done, 0);
     }
-  } else {  // ---- epilogue warps 2..5
+  } else {  // ---- epilogue warps 2..5, one output row per thread
     const int qd = warp & 3;
     const int row = qd * 32 + lane;
-    const long long t = m0 + row;
-    const bool valid = t < T;
-    const uint32_t tl = tmem_base + ((uint32_t)(qd * 32) << 16);
-    if (mbar_wait(acc_full, 0, abort_flag)) {
+    int ti = 0;
+    for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
+      const long long m0 = (tile / NT) * 128;
+      const int n0 = (int)(tile % NT) * BN;
+      const int a = ti % C::NACC;
+      const long long t = m0 + row;
+      const bool valid = t < T;
+      const uint32_t tl = tmem_base + a * C::ACC_COLS + ((uint32_t)(qd * 32) << 16);
+      if (!mbar_wait_warp(&acc_full[a], (uint32_t)(ti / C::NACC) & 1, abort_flag)) break;
       tc_fence_after();
       if constexpr (EPI == EPI_QKV) {
 #pragma unroll 1
@@ -512,6 +544,8 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
     }
   }
   __syncthreads();
