@@ -13,10 +13,12 @@
 // Two sequences are processed in lockstep, one per worker warpgroup, so the
 // tensor core alternates between them while the other one is in its
 // LayerNorm / softmax / epilogue. Per sequence slot, TMEM (256 columns):
-//   [0, 96)    q|k|v projection of one head (fp32)    -- later the out-proj acc [0, d)
+//   [0, 96)    q|k|v projection of one head (fp32)
 //   [96, 112)  q of the head as fp16 pairs (A operand of S = q k^T, read from TMEM)
 //   [96, 128)  O = P v of the head (fp32)
-//   [128, 256) S = q k^T (fp32); P (fp16 pairs) overwrites [128, 192) in place
+//   [128, 256) S = q k^T (fp32); P (fp16 pairs) overwrites [128, 192) in place;
+//              after the last head, the out-projection accumulator [128, 128 + d)
+// so the next sequence's first q|k|v projection can run during the LN2 epilogue.
 // Shared memory per slot: A = LN1(x) fp16 (kept for every head's projection),
 // C = ctx fp16 (A operand of the out-projection), k [128 x 32] and v^T [32 x 128]
 // fp16 of the current head. Weight tiles (q|k|v rows of one head, then Wo)
@@ -64,7 +66,7 @@ struct FusedCfg {
   static constexpr int PARAM_BYTES = 3 * DM * 4;     // bo, ln2_w, ln2_b in shared memory
   static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + PARAM_BYTES + 1024;
   static_assert(SMEM <= 232448, "fits the 227 KB opt-in shared memory of one CTA");
-  static_assert(4 + 2 * 16 + 4 <= 64, "barrier block fits in 512 bytes");
+  static_assert(4 + 2 * 17 + 4 <= 64, "barrier block fits in 512 bytes");
   // d = 128: the fourth 32-column chunk of x and y is staged in the weight
   // buffer that held Wo, once both slots' out-projections have read it.
   static constexpr bool WO_STAGE = DM / 32 > 3;
@@ -73,7 +75,7 @@ struct FusedCfg {
 
 enum FusedBar : int { FB_A_READY = 0, FB_A_FREE, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY,
                       FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_X0, FB_X1, FB_X2, FB_X3,
-                      FB_Y_STAGED, FB_Y_READ, FB_COUNT };
+                      FB_Y_STAGED, FB_Y_READ, FB_Y_CTX, FB_COUNT };
 
 template <int DM, bool KMASK>   // KMASK: a key-padding mask may be given
 __global__ void __launch_bounds__(512, 1)
@@ -126,7 +128,8 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(sb(s, FB_X2), 1);
       mbar_init(sb(s, FB_X3), 1);
       mbar_init(sb(s, FB_Y_STAGED), 4);   // every row warp has written its y rows
-      mbar_init(sb(s, FB_Y_READ), 1);     // the leader saw TMA finish reading them
+      mbar_init(sb(s, FB_Y_READ), 1);     // the leader saw TMA finish reading the k|v chunk
+      mbar_init(sb(s, FB_Y_CTX), 1);      // ... and the ctx chunks
     }
     mbar_init(mma_done, 2);
     mbar_init(wo_done, 2);
@@ -257,7 +260,7 @@ __global__ void __launch_bounds__(512, 1)
             for (int k = 0; k < DM / 16; ++k) {
               const uint32_t oc = (uint32_t)(k >> 2) * 16384 + (k & 3) * 32;
               const uint32_t ow = (uint32_t)(k >> 2) * (DM * 128) + (k & 3) * 32;
-              umma_f16_ss(t_slot, sdesc_kmajor(cbase + oc, 128), sdesc_kmajor(wbase + ow, 128), id_out,
+              umma_f16_ss(t_slot + 128, sdesc_kmajor(cbase + oc, 128), sdesc_kmajor(wbase + ow, 128), id_out,
                           k > 0 ? 1u : 0u);
             }
             umma_commit(sb(s, FB_OUT_FULL));
@@ -379,9 +382,9 @@ __global__ void __launch_bounds__(512, 1)
       if (seq >= a.B) break;
       const long long t0 = (long long)seq * S;
       const bool leader = (q == 0 && lane == 0);
-      if (pi > 0) {   // the previous sequence's y stores must have read k|v and ctx
+      if (pi > 0) {   // the previous sequence's y store out of k|v must have read it
         if (leader) {
-          bulk_wait_read_all();
+          bulk_wait_read<1>();   // groups: ([chunk 3]), [chunk 0: k|v], [chunks 1-2: ctx]
           mbar_arrive(sb(s, FB_Y_READ));
         }
         if (!mbar_wait_warp(sb(s, FB_Y_READ), (pi - 1) & 1, abort_flag)) break;
@@ -467,7 +470,7 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if (h < H - 1) mbar_arrive(sb(s, FB_QKV_FREE));   // the last head's is arrived after LN2
+          mbar_arrive(sb(s, FB_QKV_FREE));   // q|k|v accumulator [0, 96) read
           mbar_arrive(sb(s, FB_KQV_READY));
         }
         // ---- softmax of S = q k^T (one row per thread, exact: S <= 128 keys)
@@ -525,6 +528,13 @@ __global__ void __launch_bounds__(512, 1)
         // ---- ctx columns of head h = O / l, fp16, into the out-projection operand
         if (!mbar_wait_warp(sb(s, FB_O_FULL), n & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
+        if (h == 0 && pi > 0) {   // the previous sequence's y stores out of ctx have read it
+          if (leader) {
+            bulk_wait_read_all();
+            mbar_arrive(sb(s, FB_Y_CTX));
+          }
+          if (!mbar_wait_warp(sb(s, FB_Y_CTX), (pi - 1) & 1, abort_flag)) { ok = false; break; }
+        }
         {
           uint32_t r[32];
           tmem_ld32(tb + 96, r);
@@ -600,7 +610,7 @@ __global__ void __launch_bounds__(512, 1)
             xv[4 * c + 0] = t4.x; xv[4 * c + 1] = t4.y; xv[4 * c + 2] = t4.z; xv[4 * c + 3] = t4.w;
           }
           uint32_t r[32];
-          tmem_ld32(tb + 32 * cc, r);
+          tmem_ld32(tb + 128 + 32 * cc, r);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const int col = cc * 32 + 4 * c;
@@ -625,7 +635,7 @@ __global__ void __launch_bounds__(512, 1)
             r[4 * c + 2] = __float_as_uint(a23.x);
             r[4 * c + 3] = __float_as_uint(a23.y);
           }
-          tmem_st32(tb + 32 * cc, r);
+          tmem_st32(tb + 128 + 32 * cc, r);
         }
         // Each thread reads and later overwrites only its own row of each
         // staging buffer, so no barrier is needed between the two passes.
@@ -642,7 +652,7 @@ __global__ void __launch_bounds__(512, 1)
         // this row's x in place.
         auto write_y = [&](int cc, uint8_t* ybuf) {
           uint32_t r[32];
-          tmem_ld32(tb + 32 * cc, r);
+          tmem_ld32(tb + 128 + 32 * cc, r);
           const uint32_t dst = smem_u32(ybuf) + row * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -663,23 +673,26 @@ __global__ void __launch_bounds__(512, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_Y_STAGED));
         if (leader && mbar_wait(sb(s, FB_Y_STAGED), pi & 1, abort_flag)) {
-          if constexpr (C::WO_STAGE) {   // chunk 3 first, in its own group: it frees the weight buffer
+          // Three bulk groups, in the order their buffers are needed again:
+          // chunk 3 (the weight buffer), chunk 0 (k|v, the next sequence's
+          // first epilogue), chunks 1-2 (ctx, after its first softmax).
+          if constexpr (C::WO_STAGE) {
             tma_store_3d(&map_y, wbuf, 96, 0, seq);
             bulk_commit();
           }
-          for (int cc = 0; cc < NXC && cc < 3; ++cc) tma_store_3d(&map_y, xchunk(cc), cc * 32, 0, seq);
+          tma_store_3d(&map_y, xchunk(0), 0, 0, seq);
+          bulk_commit();
+          for (int cc = 1; cc < NXC && cc < 3; ++cc) tma_store_3d(&map_y, xchunk(cc), cc * 32, 0, seq);
           bulk_commit();
           if constexpr (C::WO_STAGE) {
-            bulk_wait_read<1>();
+            bulk_wait_read<2>();
             mbar_arrive(&w_empty[wo_b]);
           }
         }
-        // ctx and k|v are rewritten by the next sequence: the leader waits for
-        // TMA to have read them at the start of that sequence.
+        // k|v and ctx are rewritten by the next sequence: the leader waits for
+        // TMA to have read them just before (start of the sequence / first ctx).
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sb(s, FB_QKV_FREE));  // TMEM [0, d) free for the next sequence
+      tc_fence_before();   // TMEM reads of this sequence done before the next S MMA
     }
   }
   if (warp == 4 || warp == 8) {
