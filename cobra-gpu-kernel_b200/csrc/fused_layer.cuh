@@ -565,6 +565,17 @@ __global__ void __launch_bounds__(512, 1)
       // that held Wo, once both slots' out-projections have read it. y leaves
       // through the same four buffers.
       constexpr int NXC = DM / 32;                       // 4 (d=128) or 2 (d=64)
+      // Chunks per TMEM round trip in the LN2 passes: two (64 columns) where
+      // registers allow; the masked variant keeps one.
+      constexpr int CPR = KMASK ? 1 : 2;
+      auto tmem_ld_cols = [&](uint32_t taddr, uint32_t (&rr)[32 * CPR]) {
+        if constexpr (CPR == 2) tmem_ld64(taddr, rr);
+        else tmem_ld32(taddr, rr);
+      };
+      auto tmem_st_cols = [&](uint32_t taddr, uint32_t (&rr)[32 * CPR]) {
+        if constexpr (CPR == 2) tmem_st64(taddr, rr);
+        else tmem_st32(taddr, rr);
+      };
       uint8_t* xbuf = slot_k(s);
       uint8_t* cbuf = slot_c(s);
       const int wo_b = (pi * (H + 1) + H) & 1;           // ring buffer of this pair's Wo tile
@@ -599,43 +610,48 @@ __global__ void __launch_bounds__(512, 1)
         float2 sum2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);   // packed fp32x2 partials
         bool xok = true;
 #pragma unroll 1
-        for (int cc = 0; cc < NXC; ++cc) {
-          uint64_t* bar = sb(s, FB_X0 + cc);
-          const uint8_t* src = xchunk(cc);
-          if (!mbar_wait_warp(bar, pi & 1, abort_flag)) { xok = false; break; }
-          float xv[32];
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const float4 t4 = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
-            xv[4 * c + 0] = t4.x; xv[4 * c + 1] = t4.y; xv[4 * c + 2] = t4.z; xv[4 * c + 3] = t4.w;
+        for (int cp = 0; cp < NXC / CPR; ++cp) {   // CPR 32-column chunks per TMEM round trip
+          if (!mbar_wait_warp(sb(s, FB_X0 + CPR * cp), pi & 1, abort_flag) ||
+              (CPR == 2 && !mbar_wait_warp(sb(s, FB_X0 + CPR * cp + 1), pi & 1, abort_flag))) {
+            xok = false;
+            break;
           }
-          uint32_t r[32];
-          tmem_ld32(tb + 128 + 32 * cc, r);
+          uint32_t r[32 * CPR];
+          tmem_ld_cols(tb + 128 + 32 * CPR * cp, r);
+          // Columns [32*HH, 32*HH + 32) of r are chunk CPR*cp + HH (HH a
+          // literal at each call, so r stays in registers).
+          auto stats_chunk = [&](const int HH) {
+            const int cc = CPR * cp + HH;
+            const uint8_t* src = xchunk(cc);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int col = cc * 32 + 4 * c;
-            const float4 bb = *reinterpret_cast<const float4*>(sprm + col);
-            // r = x + (acc + bo), in pairs; a padded row keeps r = x.
-            float2 a01 = make_float2(xv[4 * c + 0], xv[4 * c + 1]);
-            float2 a23 = make_float2(xv[4 * c + 2], xv[4 * c + 3]);
-            if (qkeep) {
-              a01 = __fadd2_rn(a01, __fadd2_rn(make_float2(__uint_as_float(r[4 * c + 0]), __uint_as_float(r[4 * c + 1])),
-                                               make_float2(bb.x, bb.y)));
-              a23 = __fadd2_rn(a23, __fadd2_rn(make_float2(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])),
-                                               make_float2(bb.z, bb.w)));
+            for (int c = 0; c < 8; ++c) {
+              const int col = cc * 32 + 4 * c;
+              const float4 x4 = *reinterpret_cast<const float4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
+              const float4 bb = *reinterpret_cast<const float4*>(sprm + col);
+              const int i0 = 32 * HH + 4 * c;
+              // r = x + (acc + bo), in pairs; a padded row keeps r = x.
+              const float2 acc01 = make_float2(__uint_as_float(r[i0 + 0]), __uint_as_float(r[i0 + 1]));
+              const float2 acc23 = make_float2(__uint_as_float(r[i0 + 2]), __uint_as_float(r[i0 + 3]));
+              float2 a01 = make_float2(x4.x, x4.y), a23 = make_float2(x4.z, x4.w);
+              const float2 o01 = __fadd2_rn(acc01, make_float2(bb.x, bb.y));
+              const float2 o23 = __fadd2_rn(acc23, make_float2(bb.z, bb.w));
+              a01 = qkeep ? __fadd2_rn(a01, o01) : a01;
+              a23 = qkeep ? __fadd2_rn(a23, o23) : a23;
+              if (cc == 0 && c == 0) shift = a01.x;
+              const float2 nsh = make_float2(-shift, -shift);
+              const float2 d01 = __fadd2_rn(a01, nsh), d23 = __fadd2_rn(a23, nsh);
+              sum2 = __fadd2_rn(sum2, __fadd2_rn(d01, d23));
+              sq2 = __ffma2_rn(d01, d01, sq2);
+              sq2 = __ffma2_rn(d23, d23, sq2);
+              r[i0 + 0] = __float_as_uint(a01.x);
+              r[i0 + 1] = __float_as_uint(a01.y);
+              r[i0 + 2] = __float_as_uint(a23.x);
+              r[i0 + 3] = __float_as_uint(a23.y);
             }
-            if (cc == 0 && c == 0) shift = a01.x;
-            const float2 nsh = make_float2(-shift, -shift);
-            const float2 d01 = __fadd2_rn(a01, nsh), d23 = __fadd2_rn(a23, nsh);
-            sum2 = __fadd2_rn(sum2, __fadd2_rn(d01, d23));
-            sq2 = __ffma2_rn(d01, d01, sq2);
-            sq2 = __ffma2_rn(d23, d23, sq2);
-            r[4 * c + 0] = __float_as_uint(a01.x);
-            r[4 * c + 1] = __float_as_uint(a01.y);
-            r[4 * c + 2] = __float_as_uint(a23.x);
-            r[4 * c + 3] = __float_as_uint(a23.y);
-          }
-          tmem_st32(tb + 128 + 32 * cc, r);
+          };
+          stats_chunk(0);
+          if constexpr (CPR == 2) stats_chunk(1);
+          tmem_st_cols(tb + 128 + 32 * CPR * cp, r);
         }
         // Each thread reads and later overwrites only its own row of each
         // staging buffer, so no barrier is needed between the two passes.
@@ -650,25 +666,31 @@ __global__ void __launch_bounds__(512, 1)
         // came in, all in one round.
         // Second pass: y from r (kept in TMEM by the first pass), written over
         // this row's x in place.
-        auto write_y = [&](int cc, uint8_t* ybuf) {
-          uint32_t r[32];
-          tmem_ld32(tb + 128 + 32 * cc, r);
-          const uint32_t dst = smem_u32(ybuf) + row * 128;
+        auto write_y = [&](int cp) {   // chunks CPR*cp .. from one TMEM load
+          uint32_t r[32 * CPR];
+          tmem_ld_cols(tb + 128 + 32 * CPR * cp, r);
+          auto y_chunk = [&](const int HH) {   // HH a literal at each call: r stays in registers
+            const int cc = CPR * cp + HH;
+            const uint32_t dst = smem_u32(xchunk(cc)) + row * 128;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int col = cc * 32 + 4 * c;
-            const float4 wv = *reinterpret_cast<const float4*>(sprm + DM + col);
-            const float4 bb = *reinterpret_cast<const float4*>(sprm + 2 * DM + col);
-            const float2 t01 = __ffma2_rn(make_float2(__uint_as_float(r[4 * c + 0]), __uint_as_float(r[4 * c + 1])), rs2, nm2);
-            const float2 t23 = __ffma2_rn(make_float2(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])), rs2, nm2);
-            const float2 y01 = __ffma2_rn(t01, make_float2(wv.x, wv.y), make_float2(bb.x, bb.y));
-            const float2 y23 = __ffma2_rn(t23, make_float2(wv.z, wv.w), make_float2(bb.z, bb.w));
-            st_shared_v4(dst + ((c ^ (row & 7)) << 4), __float_as_uint(y01.x), __float_as_uint(y01.y),
-                         __float_as_uint(y23.x), __float_as_uint(y23.y));
-          }
+            for (int c = 0; c < 8; ++c) {
+              const int col = cc * 32 + 4 * c;
+              const int i0 = 32 * HH + 4 * c;
+              const float4 wv = *reinterpret_cast<const float4*>(sprm + DM + col);
+              const float4 bb = *reinterpret_cast<const float4*>(sprm + 2 * DM + col);
+              const float2 t01 = __ffma2_rn(make_float2(__uint_as_float(r[i0 + 0]), __uint_as_float(r[i0 + 1])), rs2, nm2);
+              const float2 t23 = __ffma2_rn(make_float2(__uint_as_float(r[i0 + 2]), __uint_as_float(r[i0 + 3])), rs2, nm2);
+              const float2 y01 = __ffma2_rn(t01, make_float2(wv.x, wv.y), make_float2(bb.x, bb.y));
+              const float2 y23 = __ffma2_rn(t23, make_float2(wv.z, wv.w), make_float2(bb.z, bb.w));
+              st_shared_v4(dst + ((c ^ (row & 7)) << 4), __float_as_uint(y01.x), __float_as_uint(y01.y),
+                           __float_as_uint(y23.x), __float_as_uint(y23.y));
+            }
+          };
+          y_chunk(0);
+          if constexpr (CPR == 2) y_chunk(1);
         };
 #pragma unroll 1
-        for (int cc = 0; cc < NXC; ++cc) write_y(cc, xchunk(cc));
+        for (int cp = 0; cp < NXC / CPR; ++cp) write_y(cp);
         fence_proxy_async_smem();   // generic writes before the async-proxy (TMA) reads
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_Y_STAGED));
