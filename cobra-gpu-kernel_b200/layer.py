@@ -9,11 +9,17 @@ lazily on the first forward (as ``UserOptimizedTransformer._prepare`` does,
 
     y = LayerNorm_2(x + Attention(LayerNorm_1(x)))
 
-through the sm_100a library (``include/cobra_b200.h``): K1 LN1+QKV GEMM,
-K2 flash attention, K3 out-proj + residual + LN2. Small inputs replay a CUDA
-graph of the three launches (the reference's ``_run_graphed``, :1331-1360).
+through the sm_100a library (``include/cobra_b200.h``): one persistent
+whole-layer kernel for d_model 64/128 with head_dim 32 and S <= 128, else K1
+LN1+QKV GEMM, K2 flash attention, K3 out-proj + residual + LN2. Inputs up to
+64 MiB replay a captured CUDA graph (the reference's ``_run_graphed``,
+:1331-1360). An optional key-padding mask follows BaselineSelfAttention
+(:106-109, :121-122).
 
-There is no CPU path: inputs must be fp32 CUDA tensors on an sm_100 device.
+The computation always runs on the GPU that holds the parameters: a
+host-resident x is streamed through it in chunks (the reference's
+``_run_streamed``, :1418-1508) and comes back as a host tensor; a layer whose
+parameters are on the CPU raises (there is no CPU path).
 """
 
 from __future__ import annotations

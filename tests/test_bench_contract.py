@@ -1,0 +1,36 @@
+"""bench.py's output contract, checked where it can run without a GPU: the
+reference arm (the reference's PyTorch layer on the host cores) prints one
+JSON line with the keys the driver reads."""
+
+import json
+import subprocess
+import sys
+
+from tests.conftest import ROOT
+
+
+def _run(*args):
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], capture_output=True, text=True,
+                       timeout=600, cwd=str(ROOT))
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    return json.loads(lines[0])
+
+
+def test_reference_arm_json_line():
+    d = _run("--impl", "reference", "--config", "cfg1", "--steps", "2", "--warmup", "1")
+    for k in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+              "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert k in d, k
+    assert d["impl"] == "reference"
+    assert d["warmup"] >= 3                       # the contract's minimum
+    assert d["value"] > 0 and d["unit"] == "tokens/s"
+    assert d["config"]["workload"] == "cfg1"
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_marks_cfg5_infeasible():
+    d = _run("--impl", "reference", "--config", "cfg5", "--steps", "1", "--warmup", "1")
+    assert d["impl"] == "reference" and "unavailable" in d and "infeasible" in d["unavailable"]
