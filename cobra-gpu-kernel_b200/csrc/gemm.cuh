@@ -140,50 +140,63 @@ __global__ void __launch_bounds__(256, 1)
   }
 
   // ---- LayerNorm prologue: 16 rows per warp, into the swizzled fp16 A tile.
+  // The loads of RB rows are issued together (RB * NV float4 per lane in
+  // flight), so a warp waits for memory once per group of rows, not per row.
   {
+    constexpr int RB = 16 / C::NV;
     const float inv_d = 1.0f / (float)d;
     const uint32_t a_base = smem_u32(sA);
+    float4 w4[C::NV], b4[C::NV];
+#pragma unroll
+    for (int i = 0; i < C::NV; ++i) {
+      const int k = (lane + 32 * i) * 4;
+      w4[i] = k < d ? __ldg(reinterpret_cast<const float4*>(ln_w + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      b4[i] = k < d ? __ldg(reinterpret_cast<const float4*>(ln_b + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll 1
-    for (int rr = 0; rr < 16; ++rr) {
-      const int row = warp * 16 + rr;
-      const long long t = m0 + row;
-      const bool valid = t < T;
-      float4 v[C::NV];
-      float s = 0.f;
+    for (int r0 = 0; r0 < 16; r0 += RB) {
+      float4 v[RB][C::NV];
 #pragma unroll
-      for (int i = 0; i < C::NV; ++i) {
-        const int k = (lane + 32 * i) * 4;
-        if (valid && k < d) {
-          v[i] = __ldg(reinterpret_cast<const float4*>(x + t * d + k));
-          s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-        } else {
-          v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int rr = 0; rr < RB; ++rr) {
+        const long long t = m0 + warp * 16 + r0 + rr;
+#pragma unroll
+        for (int i = 0; i < C::NV; ++i) {
+          const int k = (lane + 32 * i) * 4;
+          v[rr][i] = (t < T && k < d) ? ldg_stream_f4(x + t * d + k) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      const float mean = warp_sum(s) * inv_d;
-      float q = 0.f;
 #pragma unroll
-      for (int i = 0; i < C::NV; ++i) {
-        const int k = (lane + 32 * i) * 4;
-        if (valid && k < d) {
-          const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
-          q += (a * a + b * b) + (c * c + e * e);
-        }
-      }
-      const float rstd = rsqrtf(warp_sum(q) * inv_d + eps);
+      for (int rr = 0; rr < RB; ++rr) {
+        const int row = warp * 16 + r0 + rr;
+        const bool valid = m0 + row < T;
+        float s = 0.f;
 #pragma unroll
-      for (int i = 0; i < C::NV; ++i) {
-        const int k = (lane + 32 * i) * 4;
-        if (k < KP) {
-          uint32_t lo = 0, hi = 0;
-          if (valid && k < d) {
-            const float4 w4 = __ldg(reinterpret_cast<const float4*>(ln_w + k));
-            const float4 b4 = __ldg(reinterpret_cast<const float4*>(ln_b + k));
-            lo = pack_half2((v[i].x - mean) * rstd * w4.x + b4.x, (v[i].y - mean) * rstd * w4.y + b4.y);
-            hi = pack_half2((v[i].z - mean) * rstd * w4.z + b4.z, (v[i].w - mean) * rstd * w4.w + b4.w);
+        for (int i = 0; i < C::NV; ++i) s += (v[rr][i].x + v[rr][i].y) + (v[rr][i].z + v[rr][i].w);
+        const float mean = warp_sum(s) * inv_d;
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < C::NV; ++i) {
+          const int k = (lane + 32 * i) * 4;
+          if (k < d) {
+            const float a = v[rr][i].x - mean, b = v[rr][i].y - mean, c = v[rr][i].z - mean, e = v[rr][i].w - mean;
+            q += (a * a + b * b) + (c * c + e * e);
           }
-          const int kc = k >> 6, kin = k & 63;
-          st_shared_v2(a_base + kc * 16384 + swz_offset(row, kin >> 3, 128) + (kin & 7) * 2, lo, hi);
+        }
+        const float rstd = rsqrtf(warp_sum(q) * inv_d + eps);
+#pragma unroll
+        for (int i = 0; i < C::NV; ++i) {
+          const int k = (lane + 32 * i) * 4;
+          if (k < KP) {
+            uint32_t lo = 0, hi = 0;
+            if (valid && k < d) {
+              lo = pack_half2((v[rr][i].x - mean) * rstd * w4[i].x + b4[i].x,
+                              (v[rr][i].y - mean) * rstd * w4[i].y + b4[i].y);
+              hi = pack_half2((v[rr][i].z - mean) * rstd * w4[i].z + b4[i].z,
+                              (v[rr][i].w - mean) * rstd * w4[i].w + b4[i].w);
+            }
+            const int kc = k >> 6, kin = k & 63;
+            st_shared_v2(a_base + kc * 16384 + swz_offset(row, kin >> 3, 128) + (kin & 7) * 2, lo, hi);
+          }
         }
       }
     }
@@ -288,6 +301,17 @@ struct EpiArgs {
   __half* h;               // EPI_GELU output, fp16 [T, ldh]
   int ldh;
 };
+
+// Residual x of one row, columns [col0, col0 + 32), as 8 float4 (zeros past
+// lim or for rows beyond T). Issued a chunk ahead of its use, so the HBM
+// latency of one chunk overlaps the work on the previous one. The eight loads
+// of a thread share one 128-byte line, so they go through L1.
+__device__ __forceinline__ void load_x_chunk(const float* xr, int col0, bool valid, int lim, float4 (&v)[8]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    v[c] = (valid && col0 + 4 * c < lim) ? __ldg(reinterpret_cast<const float4*>(xr + col0 + 4 * c))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+}
 
 template <int BN, int ST>
 struct GemmTmaCfg {
@@ -399,6 +423,8 @@ __global__ void __launch_bounds__(192, 1)
     const int qd = warp & 3;
     const int row = qd * 32 + lane;
     int ti = 0;
+    float4 xn[8];          // EPI_RESID_LN: the next x chunk of this thread's row, loaded ahead
+    bool x_next = false;   // xn already holds the first chunk of this tile's row
     for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
       const long long m0 = (tile / NT) * 128;
       const int n0 = (int)(tile % NT) * BN;
@@ -406,6 +432,14 @@ __global__ void __launch_bounds__(192, 1)
       const long long t = m0 + row;
       const bool valid = t < T;
       const uint32_t tl = tmem_base + a * C::ACC_COLS + ((uint32_t)(qd * 32) << 16);
+      // EPI_RESID_LN: the row's first x chunk is loaded before the wait for
+      // the accumulator (x does not depend on it), or was loaded during the
+      // previous tile.
+      const float* xrow = ea.x + t * ea.d;
+      if constexpr (EPI == EPI_RESID_LN) {
+        if (!x_next) load_x_chunk(xrow, 0, valid, ea.d, xn);
+        x_next = false;
+      }
       if (!mbar_wait_warp(&acc_full[a], (uint32_t)(ti / C::NACC) & 1, abort_flag)) break;
       tc_fence_after();
       if constexpr (EPI == EPI_QKV) {
@@ -425,7 +459,7 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t r[32];
           tmem_ld32(tl + cc * 32, r);
           if (valid) {
-            const float* xr = ea.x + t * ea.d + col0;
+            const float* xr = xrow + col0;
             float* yr = ea.y + t * ea.d + col0;
             // A padded query row's attention output is zeroed (bias included):
             // y = x there (BaselineSelfAttention, :121-122); at the end of a
@@ -474,19 +508,28 @@ __global__ void __launch_bounds__(192, 1)
         }
       } else {  // EPI_RESID_LN: the whole row is in this tile (n0 == 0, BN >= d)
         const int d = ea.d;
-        const float* xr = ea.x + t * d;
         const bool keep = ea.rowmask == nullptr || (valid && ea.rowmask[t] != 0);  // see EPI_RESID
         float sum = 0.f;
         // pass 1: r = x + (acc + b), written back into TMEM; row sum.
 #pragma unroll 1
         for (int cc = 0; cc < BN / 32; ++cc) {
+          float4 xc[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) xc[c] = xn[c];
+          if (cc + 1 < BN / 32) {
+            load_x_chunk(xrow, cc * 32 + 32, valid, d, xn);
+          } else if (tile + gridDim.x < tiles) {   // the next tile's first chunk
+            const long long tn = ((tile + gridDim.x) / NT) * 128 + row;
+            load_x_chunk(ea.x + tn * d, 0, tn < T, d, xn);
+            x_next = true;
+          }
           uint32_t r[32];
           tmem_ld32(tl + cc * 32, r);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const int col = cc * 32 + 4 * c;
             if (valid && col < d) {
-              const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + col));
+              const float4 xv = xc[c];
               const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.bias + col));
               const float a0 = xv.x + (keep ? __uint_as_float(r[4 * c + 0]) + bv.x : 0.f);
               const float a1 = xv.y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
