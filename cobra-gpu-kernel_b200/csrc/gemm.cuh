@@ -39,7 +39,13 @@ __device__ __forceinline__ void qkv_store_chunk(const QkvOut& o, const float* __
   const long long bh = b * o.H + head;
   float v[32];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]) + __ldg(bqkv + col0 + i);
+  for (int i = 0; i < 8; ++i) {   // bqkv is 16-byte aligned (checked on the host), col0 % 32 == 0
+    const float4 b4 = __ldg(reinterpret_cast<const float4*>(bqkv + col0) + i);
+    v[4 * i + 0] = __uint_as_float(acc[4 * i + 0]) + b4.x;
+    v[4 * i + 1] = __uint_as_float(acc[4 * i + 1]) + b4.y;
+    v[4 * i + 2] = __uint_as_float(acc[4 * i + 2]) + b4.z;
+    v[4 * i + 3] = __uint_as_float(acc[4 * i + 3]) + b4.w;
+  }
   const bool pad_tail = (j0 + 32 == o.dh) && (o.dhp > o.dh);
   if (which < 2) {
     __half* dst = (which == 0 ? o.q : o.k) + (bh * o.S + s) * (long long)o.dhp + j0;
