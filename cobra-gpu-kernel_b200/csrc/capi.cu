@@ -76,8 +76,6 @@ int device_info(DevInfo* out) {
   return B200L_OK;
 }
 
-constexpr int kMaxSmemPerSm = 233472;   // shared memory per SM on sm_100 (228 KB)
-
 // Sets the dynamic shared memory limit of a kernel once per device.
 int ensure_smem(const void* func, int bytes) {
   int dev = 0;
@@ -254,31 +252,8 @@ int launch_gemm_tma_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
   if (rc) return rc;
   DevInfo dev;
   if ((rc = device_info(&dev))) return rc;
-  // Persistent: as many CTAs per SM as shared memory, registers and TMEM
-  // (each CTA allocates TMEM_COLS of the SM's 512 columns) allow, so a second
-  // CTA's epilogue hides the HBM latency of the first one's.
-  static std::atomic<int> per_sm{0};
-  if (per_sm.load(std::memory_order_relaxed) == 0) {
-    // Ask for a shared-memory carveout large enough for that many CTAs (the
-    // default split may leave room for one), keeping the rest as L1.
-    const int by_tmem = 512 / GemmTmaCfg<BN, ST>::TMEM_COLS;
-    const int per_cta = smem + 1024;   // + the per-CTA reservation
-    const int by_smem = kMaxSmemPerSm / per_cta;
-    const int want = by_tmem < by_smem ? by_tmem : by_smem;
-    cudaError_t e;
-    if (want > 1) {
-      const int pct = (100 * want * per_cta + kMaxSmemPerSm - 1) / kMaxSmemPerSm;
-      e = cudaFuncSetAttribute((const void*)kern, cudaFuncAttributePreferredSharedMemoryCarveout, pct < 100 ? pct : 100);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(PreferredSharedMemoryCarveout)");
-    }
-    int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 192, smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    per_sm.store(occ < 1 ? 1 : (occ < by_tmem ? occ : by_tmem), std::memory_order_relaxed);
-  }
-  const long long slots = (long long)dev.sms * per_sm.load(std::memory_order_relaxed);
-  const long long tiles = ((T + 127) / 128) * ((N + BN - 1) / BN);
-  const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
+  const long long tiles = ((T + 127) / 128) * ((N + BN - 1) / BN);   // persistent: at most one CTA per SM
+  const unsigned grid = (unsigned)(tiles < dev.sms ? tiles : dev.sms);
   kern<<<grid, 192, smem, st>>>(map_a, map_b, ea, T, K, N, reinterpret_cast<DevStatus*>(ws));
   return check_launch("gemm_tma_kernel");
 }
