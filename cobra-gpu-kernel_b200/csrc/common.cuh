@@ -342,41 +342,6 @@ __device__ __forceinline__ float ex2_approx(float x) {  // hardware 2^x (MUFU)
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA/ALU pipes, to take part of the softmax exponentials off
-// the MUFU unit (which runs at 1/8 of the FMA rate). Method: Cody-Waite style
-// range reduction x = j + f with j = round(x) obtained by adding 1.5*2^23
-// (the rounded integer lands in the low mantissa bits), 2^f for f in
-// [-0.5, 0.5] from a degree-3 polynomial whose coefficients were fitted for
-// this file by reweighted least squares on the relative error (max relative
-// error 7.5e-5 in fp32 Horner form, below the 4.9e-4 rounding of the fp16 P it
-// feeds), and 2^j by adding j to the exponent field: bits(t) << 23 equals
-// j << 23 because the magic constant's low 9 bits are zero. x is clamped to
-// >= -126 so the exponent never wraps; -inf (masked keys) gives 2^-126 ~ 0.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = x + 12582912.0f;
-  const float j = t - 12582912.0f;
-  const float f = x - j;
-  float p = fmaf(0.0551716573536396f, f, 0.2426111400127411f);
-  p = fmaf(p, f, 0.6932609677314758f);
-  p = fmaf(p, f, 0.9999280571937561f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-// The same 2^x for two values with packed fp32x2 FMA/add (sm_100): half the
-// issue slots of the scalar form for the polynomial part.
-__device__ __forceinline__ float2 ex2_poly2(float2 x) {
-  x.x = fmaxf(x.x, -126.0f);
-  x.y = fmaxf(x.y, -126.0f);
-  const float2 t = __fadd2_rn(x, make_float2(12582912.0f, 12582912.0f));
-  const float2 j = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
-  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);
-  float2 p = __ffma2_rn(make_float2(0.0551716573536396f, 0.0551716573536396f), f,
-                        make_float2(0.2426111400127411f, 0.2426111400127411f));
-  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
-  p = __ffma2_rn(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
-}
 // Three-input maximum (one sm_100 instruction).
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
   float m;
