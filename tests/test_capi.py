@@ -98,3 +98,30 @@ def test_descriptor_layout_matches_header(pkg, tmp_path, struct, cls):
                                           text=True).stdout.split()]
     assert out[0] == ctypes.sizeof(D)
     assert out[1:] == [getattr(D, n).offset for n in names]
+
+
+def _align(v, a=1024):
+    return (v + a - 1) // a * a
+
+
+@pytest.mark.parametrize("B,S,d,H,f", [(2, 128, 128, 4, 512), (3, 17, 96, 3, 200), (64, 128, 1024, 4, 4096)])
+def test_block_workspace_bytes_layout(pkg, B, S, d, H, f):
+    """The block's workspace is the layer's plus the fp32 residual x1, the
+    fp16 LN2 output h2 and the fp16 FFN hidden h1, each 1024-byte aligned."""
+    lib = pkg._lib.lib()
+    bd = pkg._lib.BlockDesc(layer=_desc(pkg, B, S, d, H), ffn_dim=f)
+    T = B * S
+    off = _align(pkg._lib.workspace_layout(B, S, d, H)["total"])
+    off = _align(off + T * d * 4)
+    off = _align(off + T * d * 2)
+    off = _align(off + T * f * 2)
+    assert lib.b200l_block_workspace_bytes(ctypes.byref(bd)) == off
+
+
+@pytest.mark.parametrize("f", [0, -8, 100, 65544])
+def test_block_rejects_bad_ffn_dim(pkg, f):
+    lib = pkg._lib.lib()
+    bd = pkg._lib.BlockDesc(layer=_desc(pkg, 2, 128, 128, 4), ffn_dim=f)
+    assert lib.b200l_block_workspace_bytes(ctypes.byref(bd)) == 0
+    assert lib.b200l_block_forward(ctypes.byref(bd), None, None, None, 0, None) == -1
+    assert "ffn_dim" in pkg._lib.last_error()
