@@ -19,9 +19,15 @@ EXPORTED = (
     "b200l_layer_forward", "b200l_qkv_ln_gemm", "b200l_flash_attn",
     "b200l_outproj_res_ln", "b200l_layer_forward_noalloc", "b200l_block_workspace_bytes",
     "b200l_block_forward", "b200l_row_layernorm", "b200l_cast_f16",
+    "b200l_kernel_workspace_bytes", "b200l_debug_arm", "b200l_noalloc_read_status",
 )
 
-ABI_VERSION = 2
+ABI_VERSION = 3
+
+# Fault-injection sites of b200l_debug_arm (test hook for the bounded waits).
+DEBUG_SITE_NONE = 0
+DEBUG_SITE_ATTN_KV = 1
+DEBUG_SITE_GEMM_OPERAND = 2
 
 # Size of the library's built-in scratch used by b200l_layer_forward_noalloc.
 NOALLOC_MAX_SCRATCH_BYTES = 64 * 1024 * 1024
@@ -89,6 +95,9 @@ def _declare(lib: ctypes.CDLL) -> None:
         "b200l_block_forward": (c_int, [P, P, P, P, c_size_t, P]),
         "b200l_row_layernorm": (c_int, [P, P, P, P, c_float, ctypes.c_int64, c_int32, P, P]),
         "b200l_cast_f16": (c_int, [P, P, ctypes.c_int64, P]),
+        "b200l_kernel_workspace_bytes": (c_size_t, [P]),
+        "b200l_debug_arm": (c_int, [P, c_int32, ctypes.c_uint64, P]),
+        "b200l_noalloc_read_status": (c_int, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -128,11 +137,20 @@ def _align(v: int, a: int) -> int:
     return (v + a - 1) // a * a
 
 
+def fused_shape(S: int, d: int, H: int) -> bool:
+    """b200l_layer_forward runs the whole-layer kernel for these shapes
+    (mirror of ``fused_shape`` in csrc/capi.cu)."""
+    return d in (64, 128) and d // H == 32 and d % H == 0 and S <= 128
+
+
 def workspace_layout(B: int, S: int, d: int, H: int) -> dict:
     """Byte offsets of the workspace regions (mirror of ``make_plan`` in csrc/capi.cu).
 
     q, k: fp16 [B*H, S, dhp]; vt: fp16 [B*H, dhp, sp]; ctx: fp16 [B*S, d];
-    h: fp16 [B*S, d] (only for d > 256)."""
+    h: fp16 [B*S, d] (only for d > 256). ``total`` is the full layout (what
+    the per-kernel entry points need), ``layer_total`` what
+    b200l_layer_forward needs (the status block alone for the whole-layer
+    kernel)."""
     dh = d // H
     dhp = 32 if dh <= 32 else 64 if dh <= 64 else 128 if dh <= 128 else 256
     sp = _align(S, 8)
@@ -148,4 +166,5 @@ def workspace_layout(B: int, S: int, d: int, H: int) -> dict:
     if d > 256:
         off = _align(off + T * d * 2, 1024)
     lay["total"] = off
+    lay["layer_total"] = 1024 if fused_shape(S, d, H) else off
     return lay

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* pv_done = bars + 11;
   uint64_t* mma_done = bars + 12;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 14);
+  WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 14);   // bars 14-15
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = args.S;
@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(p_full, 4);
     mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
-    *abort_flag = 0;
+    waitctl_init(wc, status);
     fence_barrier_init();
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_k);
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int item = blockIdx.x; item < args.num_items; item += gridDim.x, ++it) {
         const int bh = item / QT, qt = item % QT;
         const int qb = it % C::QST;
-        if (!mbar_wait(&q_empty[qb], ((it / C::QST) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(&q_empty[qb], ((it / C::QST) & 1) ^ 1, wc)) break;
         mbar_arrive_expect_tx(&q_full[qb], C::Q_BYTES);
         for (int kc = 0; kc < C::QKC; ++kc)
           tma_load_3d(sQ + qb * C::Q_BYTES + kc * 128 * C::QKROW, &map_q, &q_full[qb], kc * 64, qt * 128, bh);
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(192, 1)
         bool ok = true;
         for (int j = 0; j < nkv; ++j, ++g) {
           const int st = g % C::KVST;
-          if (!mbar_wait(&kv_empty[st], ((g / C::KVST) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&kv_empty[st], ((g / C::KVST) & 1) ^ 1, wc)) { ok = false; break; }
           mbar_arrive_expect_tx(&kv_full[st], C::K_BYTES + C::V_BYTES);
           uint8_t* k_dst = sK + st * C::K_BYTES;
           uint8_t* v_dst = sV + st * C::V_BYTES;
@@ -156,14 +156,14 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       for (int item = blockIdx.x; item < args.num_items && ok; item += gridDim.x, ++it) {
         const int qb = it % C::QST;
-        if (!mbar_wait(&q_full[qb], (it / C::QST) & 1, abort_flag)) break;
+        if (!mbar_wait(&q_full[qb], (it / C::QST) & 1, wc)) break;
         const uint32_t q_base = smem_u32(sQ + qb * C::Q_BYTES);
         const int nkv = item_nkv(item);
         for (int j = 0; j <= nkv; ++j) {
           if (j < nkv) {  // S_j = Q K_j^T
             const int st = (g + j) % C::KVST;
-            if (!mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, abort_flag)) { ok = false; break; }
-            if (g + j > 0 && !mbar_wait(s_free, (g + j - 1) & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, wc)) { ok = false; break; }
+            if (g + j > 0 && !mbar_wait(s_free, (g + j - 1) & 1, wc)) { ok = false; break; }
             tc_fence_after();
             const uint32_t k_base = smem_u32(sK + st * C::K_BYTES);
 #pragma unroll
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(192, 1)
           if (j > 0) {  // O += P_{j-1} V_{j-1}
             const int gp = g + j - 1;
             const int st = gp % C::KVST;
-            if (!mbar_wait(p_full, gp & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(p_full, gp & 1, wc)) { ok = false; break; }
             tc_fence_after();
             const uint32_t p_base = smem_u32(sP);
             const uint32_t v_base = smem_u32(sV + st * C::V_BYTES);
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int j = 0; j < nkv; ++j, ++g) {
         uint32_t kb[BN / 32];
         if (KMASK && mrow) key_mask_load<BN / 32>(mrow, j * BN, S, lane, kb);
-        if (!mbar_wait(s_full, g & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(s_full, g & 1, wc)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
 #pragma unroll
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (j > 0) {
           // P buffer and O are owned by the previous PV MMA until it completes.
-          if (!mbar_wait(pv_done, (g - 1) & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(pv_done, (g - 1) & 1, wc)) { ok = false; break; }
           tc_fence_after();
           if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (!ok) break;
       // ---- epilogue: ctx row = O / l (fp16), rows beyond S are not stored.
-      if (!mbar_wait(pv_done, (g - 1) & 1, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(pv_done, (g - 1) & 1, wc)) { ok = false; break; }
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.0f / l : 0.f;   // a row with every key masked -> 0
       const int b = bh / args.H, h = bh % args.H;
@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kAttn, 0);
+  if (threadIdx.x == 0 && waitctl_aborted(wc)) record_error(status, kErrTimeout, kAttn, 0);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);

@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* pv_done = bars + 14;   // [2]
   uint64_t* mma_done = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
+  WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 18);   // bars 18-19
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = args.S;
@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&pv_done[t], 1);
     }
     mbar_init(mma_done, 1);
-    *abort_flag = 0;
+    waitctl_init(wc, status);
     fence_barrier_init();
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_k);
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(384, 1)
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++it) {
         const int bh = item / QP, q0 = (item % QP) * 256;
         const int nqt = item_nqt(item);
-        if (!mbar_wait(q_empty, (it & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(q_empty, (it & 1) ^ 1, wc)) break;
         mbar_arrive_expect_tx(q_full, nqt * C::Q_BYTES);
         for (int t = 0; t < nqt; ++t)
           for (int kc = 0; kc < C::QKC; ++kc)
@@ -124,7 +124,10 @@ __global__ void __launch_bounds__(384, 1)
         const int nkv = item_nkv(item);
         for (int j = 0; j < nkv; ++j, ++g) {
           const int st = g % C::KVST;
-          if (!mbar_wait(&kv_empty[st], ((g / C::KVST) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&kv_empty[st], ((g / C::KVST) & 1) ^ 1, wc)) { ok = false; break; }
+          // Test hook: CTA 0 leaves out its first K / v^T load (nothing issued,
+          // so nothing to drain); the MMA issuer's bounded wait runs out.
+          if (g == 0 && blockIdx.x == 0 && wc->site == kSiteAttnKv) continue;
           mbar_arrive_expect_tx(&kv_full[st], C::K_BYTES + C::V_BYTES);
           for (int kc = 0; kc < C::QKC; ++kc)
             tma_load_3d(sK + st * C::K_BYTES + kc * BN * C::QKROW, &map_k, &kv_full[st], kc * 64, j * BN, bh);
@@ -154,10 +157,10 @@ __global__ void __launch_bounds__(384, 1)
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++it) {
         const int nqt = item_nqt(item);
         const int nkv = item_nkv(item);
-        if (!mbar_wait(q_full, it & 1, abort_flag)) break;
+        if (!mbar_wait(q_full, it & 1, wc)) break;
         for (int j = 0; j <= nkv && ok; ++j) {
           const int st = (g + j) % C::KVST;
-          if (j < nkv && !mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, abort_flag)) { ok = false; break; }
+          if (j < nkv && !mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, wc)) { ok = false; break; }
           for (int t = 0; t < nqt; ++t) {
             if (j < nkv) {  // S_t(j) = Q_t K_j^T into buffer a % 3. Its previous
               // user, allocation a - 3, had its P v enqueued before this MMA.
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(384, 1)
               const uint32_t d_o = tmem_base + C::O_COL + t * DHP;
               const uint32_t a_p = tmem_base + (uint32_t)(n % C::NSB) * 128;
               const uint32_t acc0 = j > 1 ? 1u : 0u;
-              if (!mbar_wait(&p_full[t], np[t] & 1, abort_flag)) { ok = false; break; }
+              if (!mbar_wait(&p_full[t], np[t] & 1, wc)) { ok = false; break; }
               tc_fence_after();
 #pragma unroll
               for (int k = 0; k < BN / 16; ++k)
@@ -227,7 +230,7 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t t_s = tmem_base + lane_off + (uint32_t)(n % C::NSB) * 128;
         uint32_t kb[BN / 32];
         if (KMASK && mrow) key_mask_load<BN / 32>(mrow, j * BN, S, lane, kb);
-        if (!mbar_wait(&s_full[n % C::NSB], (n / C::NSB) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(&s_full[n % C::NSB], (n / C::NSB) & 1, wc)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
         {
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(384, 1)
         l = l * alpha + ((a01.x + a01.y) + (a23.x + a23.y));
         if (j > 0 && __any_sync(0xffffffffu, rescale)) {
           // O_t is the previous P v's accumulator until that MMA completes.
-          if (!mbar_wait(&pv_done[t], (np - 1) & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < DHP / 32; ++c) {
@@ -314,7 +317,7 @@ __global__ void __launch_bounds__(384, 1)
       if (!ok) break;
       a += nqt * nkv;
       // ---- epilogue: ctx row = O / l (fp16); rows beyond S are not stored.
-      if (!mbar_wait(&pv_done[t], (np - 1) & 1, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.0f / l : 0.f;   // a row with every key masked -> 0
       const int b = bh / args.H, h = bh % args.H;
@@ -338,7 +341,7 @@ __global__ void __launch_bounds__(384, 1)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kAttn, 1);
+  if (threadIdx.x == 0 && waitctl_aborted(wc)) record_error(status, kErrTimeout, kAttn, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);

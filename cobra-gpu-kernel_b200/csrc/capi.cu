@@ -146,8 +146,14 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct Plan {
   int B, S, d, H, dh, dhp, sp;
   long long T;
-  size_t off_q, off_k, off_vt, off_ctx, off_h, total;
+  size_t off_q, off_k, off_vt, off_ctx, off_h;
+  size_t total;        // status block + every intermediate: what K1 / K2 / K3 one at a time need
+  bool fused;          // b200l_layer_forward runs the whole-layer kernel
+  size_t layer_total;  // what b200l_layer_forward needs: the status block alone when fused
 };
+
+// Whole-layer kernel for d_model in {64, 128}, head_dim 32, S <= 128.
+bool fused_shape(int S, int d, int dh) { return (d == 64 || d == 128) && dh == 32 && S <= 128; }
 
 int make_plan(const b200l_layer_desc* desc, Plan* p) {
   if (!desc) return fail(B200L_ERR_NULL_POINTER, "layer descriptor is NULL");
@@ -174,17 +180,26 @@ int make_plan(const b200l_layer_desc* desc, Plan* p) {
   p->off_h = off;
   if (d > 256) off = align_up(off + (size_t)T * d * 2, 1024);
   p->total = off;
+  // The whole-layer kernel keeps h, q, k, v and ctx on chip: it touches only
+  // the status block.
+  p->fused = fused_shape(S, d, dh);
+  p->layer_total = p->fused ? 1024 : p->total;
   return B200L_OK;
 }
 
-int check_common(const b200l_layer_desc* desc, const void* ws, size_t ws_bytes, Plan* p, DevInfo* dev) {
+// whole_layer: the caller is b200l_layer_forward (workspace sized by the path
+// it takes); otherwise a per-kernel entry point (every intermediate).
+int check_common(const b200l_layer_desc* desc, const void* ws, size_t ws_bytes, Plan* p, DevInfo* dev,
+                 bool whole_layer = false) {
   int rc = make_plan(desc, p);
   if (rc) return rc;
   if ((rc = device_info(dev))) return rc;
   if (!ws) return fail(B200L_ERR_NULL_POINTER, "workspace is NULL");
   if (reinterpret_cast<uintptr_t>(ws) % 1024) return fail(B200L_ERR_ALIGNMENT, "workspace must be 1024-byte aligned");
-  if (ws_bytes < p->total)
-    return fail(B200L_ERR_WORKSPACE_TOO_SMALL, "workspace has %zu bytes, need %zu", ws_bytes, p->total);
+  const size_t need = whole_layer ? p->layer_total : p->total;
+  if (ws_bytes < need)
+    return fail(B200L_ERR_WORKSPACE_TOO_SMALL, "workspace has %zu bytes, need %zu%s", ws_bytes, need,
+                whole_layer ? "" : " (the per-kernel entry points need b200l_kernel_workspace_bytes)");
   const void* ptrs[] = {desc->wqkv, desc->bqkv, desc->wo, desc->bo, desc->ln1_w, desc->ln1_b, desc->ln2_w, desc->ln2_b};
   const char* names[] = {"wqkv", "bqkv", "wo", "bo", "ln1_w", "ln1_b", "ln2_w", "ln2_b"};
   for (int i = 0; i < 8; ++i) {
@@ -376,9 +391,6 @@ int run_outproj(const b200l_layer_desc* desc, const Plan& p, const float* x, flo
   return launch_row_ln<false>(y, y, desc->ln2_w, desc->ln2_b, desc->eps2, p.T, p.d, st, nullptr);
 }
 
-// Whole-layer kernel for d_model in {64, 128}, head_dim 32, S <= 128.
-bool fused_eligible(const Plan& p) { return (p.d == 64 || p.d == 128) && p.dh == 32 && p.S <= 128; }
-
 template <int DM>
 int launch_fused_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, const float* x, float* y, void* ws,
                    cudaStream_t st) {
@@ -536,6 +548,12 @@ int b200l_last_error(char* buf, size_t n) {
 size_t b200l_layer_workspace_bytes(const b200l_layer_desc* desc) {
   Plan p;
   if (make_plan(desc, &p)) return 0;
+  return p.layer_total;
+}
+
+size_t b200l_kernel_workspace_bytes(const b200l_layer_desc* desc) {
+  Plan p;
+  if (make_plan(desc, &p)) return 0;
   return p.total;
 }
 
@@ -544,6 +562,16 @@ int b200l_clear_status(void* workspace, void* stream) {
   cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(DevStatus), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
   return B200L_OK;
+}
+
+int b200l_debug_arm(void* workspace, int32_t site, uint64_t wait_limit_ns, void* stream) {
+  if (!workspace) return fail(B200L_ERR_NULL_POINTER, "workspace is NULL");
+  if (site < 0 || site > kSiteGemmOperand) return fail(B200L_ERR_BAD_SHAPE, "unknown fault site %d", site);
+  if (wait_limit_ns != 0 && wait_limit_ns < 1000000ull)
+    return fail(B200L_ERR_BAD_SHAPE, "wait limit %llu ns is below 1 ms", (unsigned long long)wait_limit_ns);
+  debug_arm_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<DevStatus*>(workspace), site,
+                                                                    (unsigned long long)wait_limit_ns);
+  return check_launch("debug_arm_kernel");
 }
 
 int b200l_read_status(const void* workspace, void* stream) {
@@ -602,11 +630,11 @@ int b200l_layer_forward(const b200l_layer_desc* desc, const float* x, float* y, 
                         void* stream) {
   Plan p;
   DevInfo dev;
-  int rc = check_common(desc, workspace, ws_bytes, &p, &dev);
+  int rc = check_common(desc, workspace, ws_bytes, &p, &dev, /*whole_layer=*/true);
   if (rc) return rc;
   if ((rc = check_xy(x, y, true))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (fused_eligible(p)) return run_fused(desc, p, dev, x, y, workspace, st);
+  if (p.fused) return run_fused(desc, p, dev, x, y, workspace, st);
   if ((rc = run_qkv(desc, p, x, workspace, st))) return rc;
   if ((rc = run_attn(desc, p, dev, workspace, st))) return rc;
   return run_outproj(desc, p, x, y, workspace, st);
@@ -661,9 +689,11 @@ int b200l_cast_f16(const float* src, void* dst, int64_t n, void* stream) {
 }  // extern "C"
 
 // ===================================================================== no-alloc variant
-// b200l_layer_forward_noalloc: the same three kernels as b200l_layer_forward,
-// but the scratch they need (status block, q, k, v^T, ctx, h) lives in a
-// fixed array inside this library instead of a caller-provided workspace.
+// b200l_layer_forward_noalloc: the same kernels as b200l_layer_forward (the
+// whole-layer kernel where it applies, else K1 -> K2 -> K3), but the scratch
+// they need (status block, and for the three-kernel path q, k, v^T, ctx, h)
+// lives in a fixed array inside this library instead of a caller-provided
+// workspace.
 // It exists for callers that cannot call cudaMalloc themselves -- a plugin
 // inside a host process whose device memory is owned by its own pool, or a
 // latency-critical service that forbids allocation after start-up because
@@ -674,7 +704,12 @@ int b200l_cast_f16(const float* src, void* dst, int64_t n, void* stream) {
 // library holds it until the process exits. Device code could name it
 // directly, but in host code its name is only a host-side stand-in, so the
 // device address is looked up with cudaGetSymbolAddress on the first call on
-// each device (with that device current) and cached.
+// each device (with that device current) and cached for the life of the
+// process: after a cudaDeviceReset the module may be loaded at another
+// address, so a process that resets a device must not call this entry point
+// on it again. Device-side failures land in the status block at the start of
+// the array; b200l_noalloc_read_status reads it (the next no-alloc call on the
+// device clears it).
 static __device__ __align__(256) unsigned char g_noalloc_scratch[B200L_NOALLOC_MAX_SCRATCH_BYTES + 1024];
 
 namespace {
@@ -702,11 +737,11 @@ extern "C" int b200l_layer_forward_noalloc(const b200l_layer_desc* desc, const f
   Plan p;
   int rc = make_plan(desc, &p);
   if (rc) return rc;
-  if (p.total > (size_t)B200L_NOALLOC_MAX_SCRATCH_BYTES)
+  if (p.layer_total > (size_t)B200L_NOALLOC_MAX_SCRATCH_BYTES)
     return fail(B200L_ERR_WORKSPACE_TOO_SMALL,
                 "b200l_layer_forward_noalloc: this problem needs %zu bytes of scratch but the built-in scratch holds "
                 "%zu; call b200l_layer_forward with a workspace instead",
-                p.total, (size_t)B200L_NOALLOC_MAX_SCRATCH_BYTES);
+                p.layer_total, (size_t)B200L_NOALLOC_MAX_SCRATCH_BYTES);
   void* ws = nullptr;
   if ((rc = noalloc_scratch(&ws))) return rc;
   // The status block must start at zero for this call; everything else the
@@ -714,4 +749,11 @@ extern "C" int b200l_layer_forward_noalloc(const b200l_layer_desc* desc, const f
   cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(DevStatus), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc status)");
   return b200l_layer_forward(desc, x, y, ws, (size_t)B200L_NOALLOC_MAX_SCRATCH_BYTES, stream);
+}
+
+extern "C" int b200l_noalloc_read_status(void* stream) {
+  void* ws = nullptr;
+  int rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  return b200l_read_status(ws, stream);
 }

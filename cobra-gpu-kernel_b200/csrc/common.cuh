@@ -25,14 +25,46 @@ struct DevStatus {
   int kernel;     // which kernel recorded it (KernelId)
   int block;      // blockIdx.x of the first CTA that recorded it
   int where;      // kernel-specific wait site
-  int pad[60];
+  // Test hook, zero in normal use (b200l_clear_status zeroes the whole block):
+  // b200l_debug_arm sets a fault-injection site and a shorter per-wait limit
+  // so that a test can make a bounded wait run out without faulting the GPU.
+  int dbg_site;                    // FaultSite, or 0
+  int dbg_pad;
+  unsigned long long dbg_wait_ns;  // per-wait limit in ns, or 0 for kWaitLimitNs
+  int pad[56];
 };
 static_assert(sizeof(DevStatus) == 256, "status block is 256 bytes");
 
 enum KernelId : int { kQkvLnFused = 1, kGemmTma = 2, kAttn = 3, kOutProj = 4, kRowLn = 5, kFusedLayer = 6 };
 
+// Fault-injection sites (test hook): in CTA 0 of the named kernel, the TMA
+// producer leaves out the first load of its operand ring -- no expect_tx, no
+// copy -- so the consumer's bounded wait for that stage runs out. Nothing is
+// left in flight: every copy that was issued is drained before the CTA exits.
+enum FaultSite : int { kSiteNone = 0, kSiteAttnKv = 1, kSiteGemmOperand = 2 };
+
 constexpr int kErrTimeout = -7;                       // B200L_ERR_TIMEOUT
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+// Per-CTA wait control in shared memory: the abort flag every bounded wait
+// polls, the armed fault site and the per-wait time limit.
+struct WaitCtl {
+  int abort;
+  int site;
+  unsigned long long limit_ns;
+};
+static_assert(sizeof(WaitCtl) == 16, "two 8-byte barrier slots");
+
+// Called by one thread before the CTA's first __syncthreads.
+__device__ __forceinline__ void waitctl_init(WaitCtl* wc, const DevStatus* st) {
+  const unsigned long long lim = st->dbg_wait_ns;
+  wc->abort = 0;
+  wc->site = st->dbg_site;
+  wc->limit_ns = lim ? lim : kWaitLimitNs;
+}
+__device__ __forceinline__ bool waitctl_aborted(const WaitCtl* wc) {
+  return *reinterpret_cast<const volatile int*>(&wc->abort) != 0;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -97,17 +129,19 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // Bounded wait for the phase with the given parity. Returns false when the
 // CTA-wide abort flag is raised or the time limit runs out (which raises the
 // flag); callers then unwind instead of waiting forever.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, WaitCtl* wc) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long lim = wc->limit_ns;
+  const uint32_t hint = lim < 4000000ull ? (uint32_t)(lim / 8) : 500000u;
 #pragma unroll 1
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 4; ++i)
-      if (mbar_try_wait_sleep(bar, parity, 500000u)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
+      if (mbar_try_wait_sleep(bar, parity, hint)) return true;
+    if (waitctl_aborted(wc)) return false;
+    if (globaltimer_ns() - t0 > lim) {
+      *reinterpret_cast<volatile int*>(&wc->abort) = 1;
       return false;
     }
   }
@@ -116,8 +150,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // mbar_wait by all 32 lanes of a converged warp, with one verdict for the
 // whole warp: a warp-collective instruction after it (tcgen05.ld/st) never
 // runs with part of the warp gone.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, WaitCtl* wc) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, wc));
 }
 
 // Wait used only while unwinding: ignores the abort flag, bounded by time.

@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* w_empty = bars + 2;
   uint64_t* mma_done = bars + 4 + 2 * FB_COUNT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 2);
+  WaitCtl* wc = reinterpret_cast<WaitCtl*>(mma_done + 4);   // slots 4-5 past mma_done
   uint64_t* wo_done = mma_done + 3;   // both slots' out-projections have read Wo
   // bo | ln2_w | ln2_b, read by every row thread in the out-projection epilogue.
   float* sprm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);
@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(512, 1)
     }
     mbar_init(mma_done, 2);
     mbar_init(wo_done, 2);
-    *abort_flag = 0;
+    waitctl_init(wc, status);
     fence_barrier_init();
     tma_prefetch_desc(&map_wqkv);
     tma_prefetch_desc(&map_wo);
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(512, 1)
       for (int pair = blockIdx.x; pair < npairs && ok; pair += gridDim.x) {
         for (int t = 0; t <= H; ++t, ++wt) {
           const int b = wt & 1;
-          if (!mbar_wait(&w_empty[b], ((wt >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&w_empty[b], ((wt >> 1) & 1) ^ 1, wc)) { ok = false; break; }
           uint8_t* dst = sW + b * C::WBUF;
           if (t < H) {
             mbar_arrive_expect_tx(&w_full[b], C::WQ_BYTES);
@@ -198,9 +198,9 @@ __global__ void __launch_bounds__(512, 1)
       auto issue_qkv = [&](int h, bool active) -> bool {
         const int b = wt & 1;
         const int n = pi * H + h;
-        if (!mbar_wait(&w_full[b], (wt >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(&w_full[b], (wt >> 1) & 1, wc)) return false;
         if (active) {
-          if (n > 0 && !mbar_wait(sb(s, FB_QKV_FREE), (n - 1) & 1, abort_flag)) return false;
+          if (n > 0 && !mbar_wait(sb(s, FB_QKV_FREE), (n - 1) & 1, wc)) return false;
           tc_fence_after();
           const uint32_t wbase = smem_u32(sW + b * C::WBUF);
 #pragma unroll
@@ -222,12 +222,12 @@ __global__ void __launch_bounds__(512, 1)
       for (int pair = blockIdx.x; pair < npairs && ok; pair += gridDim.x, ++pi) {
         // slot 1 may be empty in the last pair: it still walks the weight ring
         const bool active = 2 * pair + s < a.B;
-        if (active && !mbar_wait(sb(s, FB_A_READY), pi & 1, abort_flag)) { ok = false; break; }
+        if (active && !mbar_wait(sb(s, FB_A_READY), pi & 1, wc)) { ok = false; break; }
         if (!issue_qkv(0, active)) { ok = false; break; }
         for (int h = 0; h < H && ok; ++h) {
           const int n = pi * H + h;
           if (active) {  // S = q k^T, q from TMEM
-            if (!mbar_wait(sb(s, FB_KQV_READY), n & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(sb(s, FB_KQV_READY), n & 1, wc)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int k = 0; k < 2; ++k)
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(512, 1)
           // next head's projection runs while this head's softmax does
           if (h + 1 < H && !issue_qkv(h + 1, active)) { ok = false; break; }
           if (active) {  // O = P v, P from TMEM
-            if (!mbar_wait(sb(s, FB_P_READY), n & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(sb(s, FB_P_READY), n & 1, wc)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int k = 0; k < 8; ++k)
@@ -251,9 +251,9 @@ __global__ void __launch_bounds__(512, 1)
         if (!ok) break;
         {  // out-projection: ctx Wo^T
           const int b = wt & 1;
-          if (!mbar_wait(&w_full[b], (wt >> 1) & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&w_full[b], (wt >> 1) & 1, wc)) { ok = false; break; }
           if (active) {
-            if (!mbar_wait(sb(s, FB_CTX_READY), pi & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(sb(s, FB_CTX_READY), pi & 1, wc)) { ok = false; break; }
             tc_fence_after();
             const uint32_t wbase = smem_u32(sW + b * C::WBUF);
 #pragma unroll
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(512, 1)
         }
       }
       // A of this slot is free once the previous sequence's last projection was read.
-      if (!mbar_wait(sb(s, FB_A_FREE), (pi & 1) ^ 1, abort_flag)) break;
+      if (!mbar_wait(sb(s, FB_A_FREE), (pi & 1) ^ 1, wc)) break;
       constexpr int IT = 2;   // row groups per batch: 8 rows, 2*NV loads in flight per lane
 #pragma unroll 1
       for (int r0 = rbeg; r0 < rbeg + 64; r0 += 4 * IT) {
@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(512, 1)
           bulk_wait_read<1>();   // groups: ([chunk 3]), [chunk 0: k|v], [chunks 1-2: ctx]
           mbar_arrive(sb(s, FB_Y_READ));
         }
-        if (!mbar_wait_warp(sb(s, FB_Y_READ), (pi - 1) & 1, abort_flag)) break;
+        if (!mbar_wait_warp(sb(s, FB_Y_READ), (pi - 1) & 1, wc)) break;
       }
       // Keys this row may see, one bit each: valid (mask), inside S, causal.
       // A padded query row (mask byte 0) keeps y = LN2(x): its attention
@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(512, 1)
       for (int h = 0; h < H; ++h) {
         const int n = pi * H + h;
         // ---- q|k|v of head h: bias, fp16; q -> TMEM, k and v^T -> shared memory
-        if (!mbar_wait_warp(sb(s, FB_QKV_FULL), n & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(sb(s, FB_QKV_FULL), n & 1, wc)) { ok = false; break; }
         tc_fence_after();
         {
           uint32_t r[32], pk[16];
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(512, 1)
           mbar_arrive(sb(s, FB_KQV_READY));
         }
         // ---- softmax of S = q k^T (one row per thread, exact: S <= 128 keys)
-        if (!mbar_wait_warp(sb(s, FB_S_FULL), n & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(sb(s, FB_S_FULL), n & 1, wc)) { ok = false; break; }
         tc_fence_after();
         float m8[8];   // eight independent running maxima: short dependency chains
 #pragma unroll
@@ -526,14 +526,14 @@ __global__ void __launch_bounds__(512, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_P_READY));
         // ---- ctx columns of head h = O / l, fp16, into the out-projection operand
-        if (!mbar_wait_warp(sb(s, FB_O_FULL), n & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(sb(s, FB_O_FULL), n & 1, wc)) { ok = false; break; }
         tc_fence_after();
         if (h == 0 && pi > 0) {   // the previous sequence's y stores out of ctx have read it
           if (leader) {
             bulk_wait_read_all();
             mbar_arrive(sb(s, FB_Y_CTX));
           }
-          if (!mbar_wait_warp(sb(s, FB_Y_CTX), (pi - 1) & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_warp(sb(s, FB_Y_CTX), (pi - 1) & 1, wc)) { ok = false; break; }
         }
         {
           uint32_t r[32];
@@ -587,7 +587,7 @@ __global__ void __launch_bounds__(512, 1)
         mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
         tma_load_3d(xbuf, &map_x, sb(s, FB_X0), 0, 0, seq);
       }
-      if (!mbar_wait_warp(sb(s, FB_OUT_FULL), pi & 1, abort_flag)) break;
+      if (!mbar_wait_warp(sb(s, FB_OUT_FULL), pi & 1, wc)) break;
       tc_fence_after();
       if (leader) {
         for (int cc = 1; cc < NXC && cc < 3; ++cc) {
@@ -596,7 +596,7 @@ __global__ void __launch_bounds__(512, 1)
           tma_load_3d(xchunk(cc), &map_x, bar, cc * 32, 0, seq);
         }
         if constexpr (C::WO_STAGE) {
-          if (mbar_wait(wo_done, pi & 1, abort_flag)) {
+          if (mbar_wait(wo_done, pi & 1, wc)) {
             mbar_arrive_expect_tx(sb(s, FB_X3), 16384);
             tma_load_3d(wbuf, &map_x, sb(s, FB_X3), 96, 0, seq);
           }
@@ -611,8 +611,8 @@ __global__ void __launch_bounds__(512, 1)
         bool xok = true;
 #pragma unroll 1
         for (int cp = 0; cp < NXC / CPR; ++cp) {   // CPR 32-column chunks per TMEM round trip
-          if (!mbar_wait_warp(sb(s, FB_X0 + CPR * cp), pi & 1, abort_flag) ||
-              (CPR == 2 && !mbar_wait_warp(sb(s, FB_X0 + CPR * cp + 1), pi & 1, abort_flag))) {
+          if (!mbar_wait_warp(sb(s, FB_X0 + CPR * cp), pi & 1, wc) ||
+              (CPR == 2 && !mbar_wait_warp(sb(s, FB_X0 + CPR * cp + 1), pi & 1, wc))) {
             xok = false;
             break;
           }
@@ -694,7 +694,7 @@ __global__ void __launch_bounds__(512, 1)
         fence_proxy_async_smem();   // generic writes before the async-proxy (TMA) reads
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_Y_STAGED));
-        if (leader && mbar_wait(sb(s, FB_Y_STAGED), pi & 1, abort_flag)) {
+        if (leader && mbar_wait(sb(s, FB_Y_STAGED), pi & 1, wc)) {
           // Three bulk groups, in the order their buffers are needed again:
           // chunk 3 (the weight buffer), chunk 0 (k|v, the next sequence's
           // first epilogue), chunks 1-2 (ctx, after its first softmax).
@@ -721,7 +721,7 @@ __global__ void __launch_bounds__(512, 1)
     if (lane == 0) bulk_wait_all();
   }
   __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kFusedLayer, 0);
+  if (threadIdx.x == 0 && waitctl_aborted(wc)) record_error(status, kErrTimeout, kFusedLayer, 0);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);

@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* acc_empty = bars + 6;  // [2]
   uint64_t* mma_done = bars + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 10);
+  WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 10);   // bars 10-11
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long m0 = (long long)blockIdx.x * 128;
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&acc_empty[i], 4);
     }
     mbar_init(mma_done, 1);
-    *abort_flag = 0;
+    waitctl_init(wc, status);
     fence_barrier_init();
     tma_prefetch_desc(&map_w);
   }
@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(256, 1)
       for (int n = 0; n < npro; ++n) last[n] = n;
       for (int n = C::WST; n < NT; ++n) {
         const int s = n % C::WST;
-        if (!mbar_wait(&w_empty[s], ((n / C::WST) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(&w_empty[s], ((n / C::WST) & 1) ^ 1, wc)) break;
         mbar_arrive_expect_tx(&w_full[s], C::W_BYTES);
         for (int kc = 0; kc < C::KC; ++kc)
           tma_load_2d(sW + s * C::W_BYTES + kc * 16384, &map_w, &w_full[s], kc * 64, n * 128);
@@ -231,8 +231,8 @@ __global__ void __launch_bounds__(256, 1)
       const uint32_t a_base = smem_u32(sA);
       for (int n = 0; n < NT; ++n) {
         const int s = n % C::WST, a = n & 1;
-        if (!mbar_wait(&w_full[s], (n / C::WST) & 1, abort_flag)) break;
-        if (!mbar_wait(&acc_empty[a], ((n >> 1) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(&w_full[s], (n / C::WST) & 1, wc)) break;
+        if (!mbar_wait(&acc_empty[a], ((n >> 1) & 1) ^ 1, wc)) break;
         tc_fence_after();
         const uint32_t w_base = smem_u32(sW + s * C::W_BYTES);
         for (int k = 0; k < KS; ++k) {
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(256, 1)
     const bool valid = t < T;
     for (int n = 0; n < NT; ++n) {
       const int a = n & 1;
-      if (!mbar_wait(&acc_full[a], (n >> 1) & 1, abort_flag)) break;
+      if (!mbar_wait(&acc_full[a], (n >> 1) & 1, wc)) break;
       tc_fence_after();
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kQkvLnFused, 0);
+  if (threadIdx.x == 0 && waitctl_aborted(wc)) record_error(status, kErrTimeout, kQkvLnFused, 0);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 256);
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* acc_empty = bars + 2 * ST + 2;  // [NACC], one arrival per epilogue warp
   uint64_t* mma_done = bars + 2 * ST + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 5);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * ST + 6);
+  WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 2 * ST + 6);   // 2 slots
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NT = (N + BN - 1) / BN;
@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&acc_empty[a], 4);
     }
     mbar_init(mma_done, 1);
-    *abort_flag = 0;
+    waitctl_init(wc, status);
     fence_barrier_init();
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
@@ -385,7 +385,10 @@ __global__ void __launch_bounds__(192, 1)
         const int n0 = (int)(tile % NT) * BN;
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const int s = (int)(it % ST);
-          if (!mbar_wait(&empty[s], (uint32_t)((it / ST) & 1) ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&empty[s], (uint32_t)((it / ST) & 1) ^ 1u, wc)) { ok = false; break; }
+          // Test hook: CTA 0 leaves out its first operand load (nothing issued,
+          // so nothing to drain); the MMA issuer's bounded wait runs out.
+          if (it == 0 && blockIdx.x == 0 && wc->site == kSiteGemmOperand) continue;
           mbar_arrive_expect_tx(&full[s], C::STAGE);
           uint8_t* st = smem + s * C::STAGE;
           tma_load_2d(st, &map_a, &full[s], kt * 64, (int)m0);
@@ -405,12 +408,12 @@ __global__ void __launch_bounds__(192, 1)
       for (long long tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
         const int a = ti % C::NACC;
         const int use = ti / C::NACC;   // earlier tiles that used accumulator a
-        if (use > 0 && !mbar_wait(&acc_empty[a], (use - 1) & 1, abort_flag)) break;
+        if (use > 0 && !mbar_wait(&acc_empty[a], (use - 1) & 1, wc)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + a * C::ACC_COLS;
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const int s = (int)(it % ST);
-          if (!mbar_wait(&full[s], (uint32_t)((it / ST) & 1), abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&full[s], (uint32_t)((it / ST) & 1), wc)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + s * C::STAGE);
           const uint32_t b_base = a_base + C::A_BYTES;
@@ -446,7 +449,7 @@ __global__ void __launch_bounds__(192, 1)
         if (!x_next) load_x_chunk(xrow, 0, valid, ea.d, xn);
         x_next = false;
       }
-      if (!mbar_wait_warp(&acc_full[a], (uint32_t)(ti / C::NACC) & 1, abort_flag)) break;
+      if (!mbar_wait_warp(&acc_full[a], (uint32_t)(ti / C::NACC) & 1, wc)) break;
       tc_fence_after();
       if constexpr (EPI == EPI_QKV) {
 #pragma unroll 1
@@ -598,7 +601,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) record_error(status, kErrTimeout, kGemmTma, EPI);
+  if (threadIdx.x == 0 && waitctl_aborted(wc)) record_error(status, kErrTimeout, kGemmTma, EPI);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);

@@ -107,4 +107,11 @@ __global__ void cast_f16_kernel(const float* __restrict__ src, __half* __restric
     dst[i] = __float2half_rn(src[i]);
 }
 
+// Test hook: arms a fault-injection site and a per-wait time limit in a
+// workspace's status block (read by every kernel at its start).
+__global__ void debug_arm_kernel(DevStatus* st, int site, unsigned long long wait_ns) {
+  st->dbg_site = site;
+  st->dbg_wait_ns = wait_ns;
+}
+
 }  // namespace b200l

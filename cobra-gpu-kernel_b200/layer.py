@@ -195,9 +195,13 @@ class B200TransformerLayer(nn.Module):
             ln2_w=ln2w.data_ptr(), ln2_b=ln2b.data_ptr(),
             valid_mask=mask.data_ptr() if mask is not None else None)
 
-    def _ensure_workspace(self, desc: _lib.LayerDesc, device: torch.device) -> None:
+    def _ensure_workspace(self, desc: _lib.LayerDesc, device: torch.device, stepwise: bool = False) -> None:
+        """Grow the workspace to what ``b200l_layer_forward`` needs for this
+        shape (the status block alone for the whole-layer kernel), or with
+        ``stepwise`` to what the per-kernel entry points need."""
         L = _lib.lib()
-        need = L.b200l_layer_workspace_bytes(ctypes.byref(desc))
+        fn = L.b200l_kernel_workspace_bytes if stepwise else L.b200l_layer_workspace_bytes
+        need = fn(ctypes.byref(desc))
         if need == 0:
             raise _lib.B200LError(-1, _lib.last_error())
         if self._ws is None or self._ws.device != device or self._ws_bytes < need:

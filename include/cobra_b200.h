@@ -27,10 +27,12 @@
  *   bqkv      fp32 [3d]
  *   wo        fp16 [d, d];  bo fp32 [d]
  *   ln*_w/_b  fp32 [d]
- *   workspace (bytes from b200l_layer_workspace_bytes), 1024-byte aligned,
- *             every region 1024-aligned (sp = S rounded up to 8):
+ *   workspace 1024-byte aligned, every region 1024-aligned (sp = S rounded
+ *             up to 8); b200l_kernel_workspace_bytes gives the full layout
  *             [status 256 B][q fp16 B*H*S*dhp][k fp16 B*H*S*dhp]
- *             [v^T fp16 B*H*dhp*sp][ctx fp16 T*d][h fp16 T*d, only d > 256]
+ *             [v^T fp16 B*H*dhp*sp][ctx fp16 T*d][h fp16 T*d, only d > 256],
+ *             b200l_layer_workspace_bytes what b200l_layer_forward needs (the
+ *             status block alone when the whole-layer kernel runs)
  */
 #ifndef COBRA_B200_H
 #define COBRA_B200_H
@@ -48,7 +50,7 @@
 extern "C" {
 #endif
 
-#define B200L_ABI_VERSION 2
+#define B200L_ABI_VERSION 3
 
 enum b200l_status {
     B200L_OK = 0,
@@ -98,10 +100,19 @@ B200L_API int b200l_version(void);
  * truncated to n bytes); returns the length of the full message. */
 B200L_API int b200l_last_error(char* buf, size_t n);
 
-/* Bytes of workspace b200l_layer_forward needs for this description.
+/* Bytes of workspace b200l_layer_forward needs for this description, by the
+ * path it takes: 1024 (the status block alone) when the whole-layer kernel
+ * runs (d_model 64 or 128, head_dim 32, seq_len <= 128), else the status block
+ * and every intermediate (as b200l_kernel_workspace_bytes). 0 for a bad shape.
  * Replaces the reference's live-set estimate ``_activation_bytes_per_seq``
  * (torch_transformer_benchmark.py:1364-1400), but exact. */
 B200L_API size_t b200l_layer_workspace_bytes(const b200l_layer_desc* desc);
+
+/* Bytes of workspace the per-kernel entry points (b200l_qkv_ln_gemm,
+ * b200l_flash_attn, b200l_outproj_res_ln) need: the status block and every
+ * intermediate of the layout above. Same reference counterpart as
+ * b200l_layer_workspace_bytes (:1364-1400). */
+B200L_API size_t b200l_kernel_workspace_bytes(const b200l_layer_desc* desc);
 
 /* Zeroes the status word at the start of a workspace (async on stream). */
 B200L_API int b200l_clear_status(void* workspace, void* stream);
@@ -109,6 +120,26 @@ B200L_API int b200l_clear_status(void* workspace, void* stream);
 /* Reads the status word (synchronises ``stream``): 0 when no kernel recorded a
  * failure, else the B200L_ERR_* code that was recorded. */
 B200L_API int b200l_read_status(const void* workspace, void* stream);
+
+/* Test hook for the bounded-wait path (no counterpart in the reference, whose
+ * only failure handling is the eager fallback after a failed graph capture,
+ * torch_transformer_benchmark.py:1527-1534). Arms, in the workspace's status
+ * block (async on ``stream``), a fault site and a per-wait time limit that
+ * every later kernel on this workspace reads at its start:
+ *   site B200L_DEBUG_SITE_ATTN_KV: in CTA 0 of the attention kernel for
+ *     head_dim <= 64, the TMA producer leaves out its first K / v^T load;
+ *   site B200L_DEBUG_SITE_GEMM_OPERAND: in CTA 0 of the TMA-fed GEMM (the
+ *     out-projection; also the QKV projection for d_model > 256), the
+ *     producer leaves out its first operand load.
+ * The consumer's wait for that stage then runs out after wait_limit_ns
+ * (0 = the normal 2 s; otherwise at least 1 ms), the CTA unwinds (every copy
+ * it issued is drained, its TMEM is freed), and B200L_ERR_TIMEOUT is recorded
+ * for b200l_read_status. Nothing faults, traps or hangs. b200l_clear_status
+ * disarms it. */
+#define B200L_DEBUG_SITE_NONE 0
+#define B200L_DEBUG_SITE_ATTN_KV 1
+#define B200L_DEBUG_SITE_GEMM_OPERAND 2
+B200L_API int b200l_debug_arm(void* workspace, int32_t site, uint64_t wait_limit_ns, void* stream);
 
 /* Packs nn.Linear weights into the layout above: wqkv = cast_fp16(cat(wq, wk,
  * wv)), bqkv = cat(bq, bk, bv), wo16 = cast_fp16(wo). Inputs fp32 on device.
@@ -124,7 +155,10 @@ B200L_API int b200l_pack_weights(int32_t d_model, const float* wq, const float* 
 B200L_API int b200l_layer_forward(const b200l_layer_desc* desc, const float* x, float* y,
                         void* workspace, size_t ws_bytes, void* stream);
 
-/* K1: h = LN1(x) fused into the QKV projection on tcgen05; writes q, k
+/* The per-kernel entry points below need a workspace of
+ * b200l_kernel_workspace_bytes (every intermediate).
+ *
+ * K1: h = LN1(x) fused into the QKV projection on tcgen05; writes q, k
  * ([B,H,S,dhp] fp16) and v^T ([B,H,dhp,S] fp16) into the workspace.
  * Replaces ``_tl_add_ln`` (:539-569, used at :1220-1223) + ``F.linear``/
  * ``_gemm_kernel`` for qkv (:283-381, :1234). */
@@ -199,10 +233,22 @@ B200L_API int b200l_cast_f16(const float* src, void* dst, int64_t n, void* strea
  *     array is cleared (cudaMemsetAsync) at the start of every call.
  *   - All calls on a device share the one array and it keeps the last call's
  *     contents: calls that overlap on the GPU (different streams without
- *     ordering between them) race and corrupt each other's results. */
+ *     ordering between them) race and corrupt each other's results.
+ *   - A device-side failure (B200L_ERR_TIMEOUT) of a call is recorded in the
+ *     array's status block: read it with b200l_noalloc_read_status before the
+ *     next no-alloc call on that device, which clears it.
+ *   - The device address is looked up once per device and kept for the life
+ *     of the process; do not call this entry point on a device again after a
+ *     cudaDeviceReset of it. */
 #define B200L_NOALLOC_MAX_SCRATCH_BYTES (64u * 1024u * 1024u)
 B200L_API int b200l_layer_forward_noalloc(const b200l_layer_desc* desc, const float* x, float* y,
                                           void* stream);
+
+/* Status of the last b200l_layer_forward_noalloc call(s) on the current
+ * device, as b200l_read_status reads a workspace (synchronises ``stream``): 0,
+ * or the B200L_ERR_* code a kernel recorded. No counterpart in the reference
+ * (see b200l_layer_forward_noalloc). */
+B200L_API int b200l_noalloc_read_status(void* stream);
 
 #ifdef __cplusplus
 }

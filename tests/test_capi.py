@@ -41,9 +41,15 @@ def _desc(pkg, B, S, d, H):
 def test_workspace_bytes_matches_python_layout(pkg, B, S, d, H):
     lib = pkg._lib.lib()
     d_ = _desc(pkg, B, S, d, H)
-    n = lib.b200l_layer_workspace_bytes(ctypes.byref(d_))
-    assert n == pkg._lib.workspace_layout(B, S, d, H)["total"]
+    lay = pkg._lib.workspace_layout(B, S, d, H)
+    n = lib.b200l_kernel_workspace_bytes(ctypes.byref(d_))
+    assert n == lay["total"]
     assert n % 1024 == 0
+    # b200l_layer_forward's workspace follows the path it takes: the status
+    # block alone for the whole-layer kernel, the full layout otherwise.
+    nl = lib.b200l_layer_workspace_bytes(ctypes.byref(d_))
+    assert nl == lay["layer_total"]
+    assert nl == (1024 if pkg._lib.fused_shape(S, d, H) else n)
 
 
 @pytest.mark.parametrize("B,S,d,H,code,msg", [
@@ -57,6 +63,7 @@ def test_bad_shapes_are_rejected_on_the_host(pkg, B, S, d, H, code, msg):
     lib = pkg._lib.lib()
     d_ = _desc(pkg, B, S, d, H)
     assert lib.b200l_layer_workspace_bytes(ctypes.byref(d_)) == 0
+    assert lib.b200l_kernel_workspace_bytes(ctypes.byref(d_)) == 0
     rc = lib.b200l_layer_forward(ctypes.byref(d_), None, None, None, 0, None)
     assert rc == code
     assert msg in pkg._lib.last_error()

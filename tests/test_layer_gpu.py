@@ -75,7 +75,7 @@ def run_stepwise(pkg, lay, x):
     B, S, d = x.shape
     pk = lay._ensure_pack(x.device)
     desc = lay._desc(B, S, pk)
-    lay._ensure_workspace(desc, x.device)
+    lay._ensure_workspace(desc, x.device, stepwise=True)
     L = pkg._lib.lib()
     st = torch.cuda.current_stream().cuda_stream
     y = torch.empty_like(x)
