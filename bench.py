@@ -4,22 +4,34 @@
 Metric: layer tokens/s = B*S / latency, the reference
 harness's definition (torch_transformer_benchmark.py:1906-1908).
 
-Default workload: BASELINE cfg2 -- B=10000, S=128, d_model=128, H=4 (d_h=32),
-x fp32 ~ N(0,1), seeded default nn.Linear init, LayerNorm gamma=1 beta=0, no
-mask, non-causal. One step = one layer forward over the batch. The input
-(655 MB) and output are larger than the 126 MB L2, so no flush is needed
-between steps.
+Default workload: BASELINE cfg5, the configuration ``north_star``'s target is
+stated on -- B=32, S=100000, d_model=1024, H=16 (d_h=64), x fp32 ~ N(0,1),
+seeded default nn.Linear init, LayerNorm gamma=1 beta=0, no mask,
+non-causal. One step = one layer forward over the batch (x and y 13.1 GB
+each, far larger than the 126 MB L2, so no flush is needed between steps).
+``--config cfg1..cfg4`` selects the other BASELINE shapes.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5] [--impl ours|reference]
 
-Multi-GPU (one process per GPU under torchrun): sequences are independent,
-so every rank runs its own full cfg batch (weak scaling) with no data-path
-collective; the timed region is bracketed by barriers and the reported time
-is the max over ranks of the CUDA-event time.
+Multi-GPU (one process per GPU under torchrun): strong scaling. The config's
+global batch is split into contiguous shards of ceil(B/N) sequences
+(``sharding.batch_shards``; cfg5 at N=8: 4 sequences per GPU). ``value`` is the
+global B*S divided by the max over ranks of the CUDA-event time of K steps
+with the shards already on their GPUs (no data-path collective: sequences are
+independent). ``e2e`` is the public API from host memory: at N=1
+``B200TransformerLayer.forward`` on a pinned host x (chunks streamed through
+the GPU, both copy directions overlapped with the kernels); at N>1
+``ShardedLayer.forward`` on rank 0's pinned host x (pieces copied to rank 0's
+GPU, sent to their ranks over NCCL, computed, sent back and copied to rank
+0's host), max over ranks of the device time around the call.
 
-``--impl reference`` times the reference's PyTorch layer on the host CPU
-(all threads) -- the oracle port of BaselineSelfAttention + nn.LayerNorm --
-on a bounded sample of the same workload; only rank 0 runs it.
+``--impl reference`` times the reference's own CPU algorithm on the host
+(all threads), only on rank 0: for cfg1-cfg4 the reference's PyTorch layer
+(the oracle port of BaselineSelfAttention + nn.LayerNorm) on a bounded sample
+of the batch; for cfg5, where that layer would materialise [B,H,S,S] scores
+(19,073 GiB, infeasible), the reference's streamed formulation
+(tools/reference_chunked.py:73-128, restated in fp32) on a sample of query
+rows of one sequence.
 """
 
 from __future__ import annotations
@@ -45,8 +57,11 @@ CONFIGS = {
     "cfg4": dict(B=64, S=1024, d=128, H=4),
     "cfg5": dict(B=32, S=100000, d=1024, H=16),
 }
+DEFAULT_CONFIG = "cfg5"
 METRIC = "layer tokens/s (B*S/latency)"
 L2_BYTES = 126 * 1024 * 1024
+SEED = 1234
+X_SEED = 1234 + 100000      # the harness times on seed + 100000 (torch_transformer_benchmark.py:1874)
 
 
 def peaks():
@@ -64,9 +79,8 @@ def fused_eligible(cfg) -> bool:
     return cfg["d"] in (64, 128) and cfg["d"] // cfg["H"] == 32 and cfg["S"] <= 128
 
 
-def kernel_work(cfg):
+def kernel_work(B, S, d):
     """Algorithmic bytes and FLOPs per launch of each kernel (per-token figures x T)."""
-    B, S, d = cfg["B"], cfg["S"], cfg["d"]
     T = B * S
     return {
         # whole layer in one kernel: x read + y write (8d B/token); 8*T*d^2 + 4*B*S^2*d FLOP
@@ -81,7 +95,7 @@ def kernel_work(cfg):
 
 
 def read_traffic(kernel: str, cfg_name: str):
-    """DRAM bytes per launch from the committed ncu summary, or None."""
+    """DRAM bytes per full-config launch from the committed ncu summary, or None."""
     p = ROOT / "profiles" / "dram_traffic.txt"
     if not p.exists():
         return None
@@ -141,11 +155,13 @@ class ClockSampler:
             return None
         sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
         mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        pw = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower().startswith("active")})
         loaded = [s for s in sm if mx and s >= 0.3 * max(mx)] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows),
+                "power_w_median": statistics.median(pw) if pw else None}
 
 
 def dist_env():
@@ -155,20 +171,31 @@ def dist_env():
     return ws, rank, local
 
 
-def cpu_reference(cfg, cfg_name, steps, warmup, budget_s=20.0):
-    """The reference's PyTorch layer on the host CPU (oracle port), bounded sample."""
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return ""
+
+
+def scores_infeasible(cfg) -> bool:
+    """The reference layer materialises [b, H, S, S] fp32 scores per call."""
+    return 4.0 * cfg["H"] * cfg["S"] ** 2 > 64e9
+
+
+def cpu_reference_layer(cfg, cfg_name, steps, warmup, budget_s=20.0):
+    """The reference's PyTorch layer on the host CPU (oracle port), bounded sample of the batch."""
     from oracle import TransformerConfig, build_reference_layer, generate_random_case
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     B, S, d, H = cfg["B"], cfg["S"], cfg["d"], cfg["H"]
-    # Score tensor [b,H,S,S] fp32 must fit: cfg5 materialises 19,073 GiB -> infeasible.
-    if 4.0 * H * S * S > 64e9:
-        return None
-    sample_b = B
     tc = TransformerConfig(1, S, d, H)
-    layer = build_reference_layer(tc, 1234)
+    layer = build_reference_layer(tc, SEED)
     # Calibrate: time one sequence, size the per-step sample to ~budget/(steps+warmup).
-    x1, _ = generate_random_case(tc, 1234 + 100000)
+    x1, _ = generate_random_case(tc, X_SEED)
     with torch.inference_mode():
         layer(x1)
         t0 = time.perf_counter()
@@ -176,8 +203,7 @@ def cpu_reference(cfg, cfg_name, steps, warmup, budget_s=20.0):
         per_seq = max(time.perf_counter() - t0, 1e-6)
     per_step = budget_s / max(1, steps + warmup)
     sample_b = int(max(1, min(B, per_step / per_seq)))
-    tcs = TransformerConfig(sample_b, S, d, H)
-    xs, _ = generate_random_case(tcs, 1234 + 100000)
+    xs, _ = generate_random_case(TransformerConfig(sample_b, S, d, H), X_SEED)
     times = []
     with torch.inference_mode():
         for i in range(warmup + steps):
@@ -187,37 +213,74 @@ def cpu_reference(cfg, cfg_name, steps, warmup, budget_s=20.0):
             if i >= warmup:
                 times.append(dt)
     med = statistics.median(times)
-    cpu_model = ""
-    try:
-        for line in Path("/proc/cpuinfo").read_text().splitlines():
-            if line.startswith("model name"):
-                cpu_model = line.split(":", 1)[1].strip()
-                break
-    except OSError:
-        pass
     return {"value": sample_b * S / med, "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"{sample_b} of {B} sequences of {cfg_name} per step (S={S}, d={d}, H={H}), fp32, "
-                      f"median of {steps} after {warmup} warm-up, {cpu_model}",
+                      f"median of {steps} after {warmup} warm-up, {cpu_model()}",
             "ms_per_step": med * 1e3}
+
+
+def cpu_reference_streamed(cfg, cfg_name, steps, warmup, rows_per_step=256):
+    """cfg5: the reference layer cannot run (its scores would be 19,073 GiB), so
+    the reference's own long-sequence formulation is timed instead: the
+    streamed restatement of tools/reference_chunked.py:73-128 in fp32 on all
+    host threads. Per step, one sequence: LN1 + the K / V projections of all S
+    keys (t_kv), then ``rows_per_step`` query rows through the Q projection,
+    the softmax over all S keys, the out-projection and LN2 (t_rows). Every
+    token costs the same, so a whole sequence takes t_kv + (S / rows) * t_rows."""
+    from oracle import TransformerConfig, build_reference_layer, streamed_keys, streamed_ctx_rows, \
+        streamed_output_rows
+    from oracle.ref_layer import sample_rows
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    B, S, d, H = cfg["B"], cfg["S"], cfg["d"], cfg["H"]
+    layer = build_reference_layer(TransformerConfig(1, S, d, H), SEED)
+    g = torch.Generator().manual_seed(X_SEED)
+    xs = torch.randn(S, d, generator=g)
+    per_seq = []
+    with torch.inference_mode():
+        for i in range(warmup + steps):
+            rows = sample_rows(S, rows_per_step, seed=i)
+            t0 = time.perf_counter()
+            h, k, v = streamed_keys(layer, xs, torch.float32)
+            t1 = time.perf_counter()
+            ctx = streamed_ctx_rows(layer, h, k, v, rows, False)
+            streamed_output_rows(layer, xs, ctx, rows)
+            t2 = time.perf_counter()
+            if i >= warmup:
+                per_seq.append((t1 - t0) + (S / rows.numel()) * (t2 - t1))
+            del h, k, v, ctx
+    med = statistics.median(per_seq)
+    return {"value": S / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{cfg_name}: the reference layer's [B,H,S,S] scores would take "
+                      f"{4.0 * H * S * S * B / 2**30:.0f} GiB (infeasible); timed instead: the streamed "
+                      f"formulation of tools/reference_chunked.py in fp32, one sequence per step (LN1 + K/V "
+                      f"projections of all {S} keys, then {rows_per_step} query rows through attention over "
+                      f"all keys, out-proj and LN2), extrapolated per sequence as t_kv + (S/rows)*t_rows; "
+                      f"median of {steps} after {warmup} warm-up, {cpu_model()}",
+            "ms_per_step": med * 1e3 * B,
+            "reference_layer": "infeasible: [B,H,S,S] scores"}
+
+
+def cpu_reference(cfg, cfg_name, steps, warmup):
+    if scores_infeasible(cfg):
+        return cpu_reference_streamed(cfg, cfg_name, steps, warmup)
+    return cpu_reference_layer(cfg, cfg_name, steps, warmup)
 
 
 def run_reference_arm(args, cfg):
     ws, rank, _ = dist_env()
     if rank != 0:
         return 0
-    r = cpu_reference(cfg, args.config, args.steps, args.warmup)
-    if r is None:
-        print(json.dumps({"impl": "reference", "unavailable":
-                          f"{args.config}: the reference materialises [B,H,S,S] scores "
-                          f"({4.0 * cfg['H'] * cfg['S'] ** 2 * cfg['B'] / 2**30:.0f} GiB), infeasible on the host"}))
-        return 0
+    r = cpu_reference(cfg, args.config, max(1, min(args.steps, 5)), max(1, min(args.warmup, 2)))
     line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: x ~ N(0,1) fp32, seeded default nn.Linear init",
-            "config": {"workload": args.config, **cfg, "causal": False, "sample_sequences_note": r["sample"]},
+            "config": {"workload": args.config, **cfg, "causal": False, "sample_note": r["sample"]},
             "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if "reference_layer" in r:
+        line["reference_layer"] = r["reference_layer"]
     print(json.dumps(line))
     return 0
 
@@ -236,10 +299,10 @@ def run_stack(args, cfg) -> int:
     f = args.ffn or 4 * d
     L = args.layers
     ocfg = OCfg(B, S, d, H, ffn_dim=f, num_layers=L)
-    ref = build_reference_transformer(ocfg, 1234)
+    ref = build_reference_transformer(ocfg, SEED)
     model = pkg.B200Transformer(pkg.TransformerConfig(B, S, d, H, ffn_dim=f, num_layers=L)).to(dev).eval()
     model.load_state_dict(ref.state_dict(), strict=True)
-    g = torch.Generator(device="cpu").manual_seed(1234 + 100000)
+    g = torch.Generator(device="cpu").manual_seed(X_SEED)
     x = torch.randn(B, S, d, generator=g).to(dev)
     big = x.numel() * 4 > L2_BYTES
     flush = None if big else torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
@@ -268,7 +331,7 @@ def run_stack(args, cfg) -> int:
     print(json.dumps({
         "metric": "stack tokens/s (B*S/latency)", "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate, fp32 in/out",
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate, fp32 in/out",
         "data": "synthetic: x ~ N(0,1) fp32, seeded default init of the reference's BaselineTransformer",
         "config": {"workload": f"{args.config} shape, {L} blocks, ffn_dim {f}", **cfg, "layers": L, "ffn_dim": f,
                    "l2": "inputs larger than L2" if big else "L2 flushed between steps"},
@@ -280,16 +343,36 @@ def run_stack(args, cfg) -> int:
     return 0
 
 
+def seeded_batch(b0: int, b1: int, S: int, d: int, device) -> torch.Tensor:
+    """Sequences [b0, b1) of the global synthetic batch, each drawn on the
+    device from its own seeded generator (so every rank builds exactly its
+    shard, and any sharding sees the same global x)."""
+    x = torch.empty(b1 - b0, S, d, dtype=torch.float32, device=device)
+    g = torch.Generator(device=device)
+    for b in range(b0, b1):
+        g.manual_seed(X_SEED + b)
+        x[b - b0].normal_(generator=g)
+    return x
+
+
+def shard_pieces(per_rank_b: int, S: int, d: int) -> int:
+    """Pieces per rank for the scatter / gather: about 16 MiB of x or more
+    each, at most 16 (a peer computes piece i while piece i+1 arrives)."""
+    return int(min(16, max(1, per_rank_b * S * d * 4 // (16 * 1024 * 1024))))
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--shard-chunks", type=int, default=2,
-                    help="pieces per rank for the scatter/gather measurement (N > 1)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement (profiling runs)")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--shard-chunks", type=int, default=0,
+                    help="pieces per rank for the N > 1 scatter / gather (0: about 16 MiB each)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (smaller cases for ncu captures)")
     ap.add_argument("--model", default="layer", choices=["layer", "stack"],
@@ -311,12 +394,12 @@ def main() -> int:
     import datetime
     import torch.distributed as dist
     import __graft_entry__
-    from oracle import TransformerConfig, build_reference_layer, generate_random_case
+    from oracle import TransformerConfig, build_reference_layer
 
     world, rank, local = dist_env()
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -324,149 +407,158 @@ def main() -> int:
     L = pkg._lib.lib()
 
     B, S, d, H = cfg["B"], cfg["S"], cfg["d"], cfg["H"]
+    shards = pkg.batch_shards(B, world)
+    a, b = shards[rank]
+    Bl = b - a                       # this rank's sequences
     T = B * S
-    tc = TransformerConfig(B, S, d, H)
-    ref = build_reference_layer(tc, 1234)
+    ref = build_reference_layer(TransformerConfig(1, S, d, H), SEED)
     layer = pkg.B200TransformerLayer(d, H, use_graphs=False).to(dev).eval()
     layer.load_state_dict(ref.state_dict(), strict=True)
-    x_host, _ = generate_random_case(tc, 1234 + 100000 + rank)
-    x = x_host.to(dev)
-    y = torch.empty_like(x)
     stream = torch.cuda.current_stream(dev)
-    pk = layer._ensure_pack(dev)
-    desc = layer._desc(B, S, pk)
-    layer._ensure_workspace(desc, dev)
-    wsp, wsb, st = layer.workspace_ptr, layer._ws_bytes, stream.cuda_stream
-
     fused = fused_eligible(cfg)
-
-    def step_kernels(ev=None):
-        if fused:   # the product path: one whole-layer kernel
-            if ev is not None:
-                ev[0].record(stream)
-            pkg._lib.check(L.b200l_layer_forward(ctypes.byref(desc), x.data_ptr(), y.data_ptr(), wsp, wsb, st))
-            if ev is not None:
-                ev[3].record(stream)
-            return
-        if ev is not None:
-            ev[0].record(stream)
-        pkg._lib.check(L.b200l_qkv_ln_gemm(ctypes.byref(desc), x.data_ptr(), wsp, wsb, st))
-        if ev is not None:
-            ev[1].record(stream)
-        pkg._lib.check(L.b200l_flash_attn(ctypes.byref(desc), wsp, wsb, st))
-        if ev is not None:
-            ev[2].record(stream)
-        pkg._lib.check(L.b200l_outproj_res_ln(ctypes.byref(desc), x.data_ptr(), y.data_ptr(), wsp, wsb, st))
-        if ev is not None:
-            ev[3].record(stream)
-
+    k_ms, total_ms = {}, 0.0
     launches_per_step = 1 if fused else 3 + (2 if d > 256 else 0)
 
     with torch.inference_mode():
-        for _ in range(args.warmup):
-            step_kernels()
-        torch.cuda.synchronize(dev)
-        layer.check_status()
+        if Bl > 0:
+            x = seeded_batch(a, b, S, d, dev)
+            y = torch.empty_like(x)
+            pk = layer._ensure_pack(dev)
+            desc = layer._desc(Bl, S, pk)
+            layer._ensure_workspace(desc, dev, stepwise=not fused)
+            wsp, wsb, st = layer.workspace_ptr, layer._ws_bytes, stream.cuda_stream
 
+        def step_kernels(ev=None):
+            """One layer forward: the whole-layer kernel, or K1 -> K2 -> K3 one
+            entry point at a time (the same launches b200l_layer_forward
+            makes), with events between them for the per-kernel times."""
+            if fused:
+                if ev is not None:
+                    ev[0].record(stream)
+                pkg._lib.check(L.b200l_layer_forward(ctypes.byref(desc), x.data_ptr(), y.data_ptr(), wsp, wsb, st))
+                if ev is not None:
+                    ev[3].record(stream)
+                return
+            if ev is not None:
+                ev[0].record(stream)
+            pkg._lib.check(L.b200l_qkv_ln_gemm(ctypes.byref(desc), x.data_ptr(), wsp, wsb, st))
+            if ev is not None:
+                ev[1].record(stream)
+            pkg._lib.check(L.b200l_flash_attn(ctypes.byref(desc), wsp, wsb, st))
+            if ev is not None:
+                ev[2].record(stream)
+            pkg._lib.check(L.b200l_outproj_res_ln(ctypes.byref(desc), x.data_ptr(), y.data_ptr(), wsp, wsb, st))
+            if ev is not None:
+                ev[3].record(stream)
+
+        if Bl > 0:
+            for _ in range(args.warmup):
+                step_kernels()
+            torch.cuda.synchronize(dev)
+            layer.check_status()
         evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
-        clk = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
-                           if os.environ.get("CUDA_VISIBLE_DEVICES") else local) if rank == 0 else None
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        gpu_index = int(vis.split(",")[local]) if vis else local
+        clk = ClockSampler(gpu_index) if rank == 0 else None
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
         if clk:
             clk.start()
             time.sleep(0.3)
-        for i in range(args.steps):
-            step_kernels(evs[i])
+        if Bl > 0:
+            for i in range(args.steps):
+                step_kernels(evs[i])
         torch.cuda.synchronize(dev)
         clocks = clk.stop() if clk else None
-        total_ms = evs[0][0].elapsed_time(evs[-1][3])
-        if fused:
-            k_ms = {"fused_layer": statistics.fmean(e[0].elapsed_time(e[3]) for e in evs)}
-        else:
-            k_ms = {name: statistics.fmean(e[i].elapsed_time(e[i + 1]) for e in evs)
-                    for i, name in enumerate(["qkv_ln_gemm", "flash_attn", "outproj_res_ln"])}
-        layer.check_status()
+        if Bl > 0:
+            total_ms = evs[0][0].elapsed_time(evs[-1][3])
+            if fused:
+                k_ms = {"fused_layer": statistics.fmean(e[0].elapsed_time(e[3]) for e in evs)}
+            else:
+                k_ms = {name: statistics.fmean(e[i].elapsed_time(e[i + 1]) for e in evs)
+                        for i, name in enumerate(["qkv_ln_gemm", "flash_attn", "outproj_res_ln"])}
+            layer.check_status()
         if world > 1:
             t = torch.tensor([total_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             total_ms = float(t.item())
             dist.barrier()
+        if Bl > 0:
+            del x, y
+        torch.cuda.empty_cache()
 
-        # ---- end to end through the public API: pinned host x -> forward ->
-        # host y (the module streams a host-resident batch through the GPU,
-        # copies in both directions overlapped with the kernels).
-        xh = x_host.pin_memory()
-        for _ in range(2):
-            yh = layer(xh)
-        torch.cuda.synchronize(dev)
-        e2e_steps = max(3, min(args.steps, 10))
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(e2e_steps):
-            yh = layer(xh)
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        e2e_ms = e0.elapsed_time(e1) / e2e_steps
-        if world > 1:
-            t = torch.tensor([e2e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
-
-        # ---- N > 1: the config's own batch held on rank 0's device, split by
-        # ShardedLayer (x slices sent, y slices gathered back over NCCL
-        # send/recv). Strong scaling; reported beside the weak-scaling value.
-        sharded = None
-        if world > 1:
-            del xh, yh
-            sl = pkg.ShardedLayer(layer, src=0, chunks=args.shard_chunks)
-            xg = x if rank == 0 else None
-            for _ in range(2):
-                sl(xg)
-            torch.cuda.synchronize(dev)
-            sh_steps = max(3, min(args.steps, 10))
-            dist.barrier()
-            torch.cuda.synchronize(dev)
-            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            for _ in range(sh_steps):
-                sl(xg)
-            s1.record(stream)
+        # ---- end to end through the public API, from and to pinned host memory.
+        e2e = None
+        if not args.no_e2e:
+            if world == 1:
+                xh = torch.empty(B, S, d, dtype=torch.float32, pin_memory=True)
+                for c0 in range(0, B, 8):
+                    xh[c0:c0 + 8].copy_(seeded_batch(c0, min(B, c0 + 8), S, d, dev))
+                call = lambda: layer(xh)                                              # noqa: E731
+                path = ("B200TransformerLayer.forward(pinned host x) -> pinned host y: chunks of "
+                        "host_chunk_seqs() sequences streamed through the GPU, both copy directions "
+                        "overlapped with the kernels")
+            else:
+                chunks = args.shard_chunks or shard_pieces(-(-B // world), S, d)
+                sl = pkg.ShardedLayer(layer, src=0, chunks=chunks)
+                xh = None
+                if rank == 0:
+                    xh = torch.empty(B, S, d, dtype=torch.float32, pin_memory=True)
+                    for c0 in range(0, B, 8):
+                        xh[c0:c0 + 8].copy_(seeded_batch(c0, min(B, c0 + 8), S, d, dev))
+                call = lambda: sl(xh)                                                 # noqa: E731
+                path = (f"ShardedLayer.forward(pinned host x on rank 0) -> pinned host y on rank 0: "
+                        f"{chunks} pieces per rank copied to rank 0's GPU, sent over NCCL, computed, sent "
+                        f"back and copied to the host on a separate stream")
+            call()                                    # warm: buffers, pinned output, kernels
             torch.cuda.synchronize(dev)
             layer.check_status()
-            t = torch.tensor([s0.elapsed_time(s1) / sh_steps], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            sh_ms = float(t.item())
-            sharded = {"value": T / (sh_ms / 1e3), "unit": "tokens/s", "ms_per_step": sh_ms,
-                       "global_batch": B, "per_gpu_batch": -(-B // world), "chunks": args.shard_chunks,
-                       "scaling": "strong", "steps": sh_steps,
-                       "path": "ShardedLayer.forward: x on rank 0's device, slices over NCCL "
-                               "send/recv, y gathered into rank 0's output"}
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.e2e_steps):
+                call()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            layer.check_status()
+            e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+            if world > 1:
+                t = torch.tensor([e2e_ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                e2e_ms = float(t.item())
+            e2e = {"value": T / (e2e_ms / 1e3), "unit": "tokens/s",
+                   "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
+                   "ms_per_step": e2e_ms, "steps": args.e2e_steps, "path": path}
 
     ms_per_step = total_ms / args.steps
-    value = world * T / (ms_per_step / 1e3)
+    value = T / (ms_per_step / 1e3)
     pk_ = peaks()
-    work = kernel_work(cfg)
     flops_layer = 8.0 * T * d * d + 4.0 * B * S * S * d
     bytes_layer = 8.0 * T * d
-    # Dominant kernel = the one with the largest share of the step.
-    dom = max(k_ms, key=k_ms.get)
-    hbm_bound = args.config in ("cfg1", "cfg2")
-    if hbm_bound:
-        achieved = work[dom]["bytes"] / (k_ms[dom] / 1e3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": pk_["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk_["hbm_gbs"], "kernel": dom,
-                "traffic": read_traffic(dom, args.config), "peak_source": pk_["source"]}
-    else:
-        achieved = work[dom]["flops"] / (k_ms[dom] / 1e3) / 1e12
-        pk_t = pk_["bf16_tflops_sustained"] if ms_per_step > 100 else pk_["bf16_tflops"]
-        roof = {"bound": "tensor", "achieved": achieved, "peak": pk_t, "unit": "TFLOP/s",
-                "frac": achieved / pk_t, "kernel": dom,
-                "traffic": read_traffic(dom, args.config), "peak_source": pk_["source"]}
+    roof = None
+    if k_ms:
+        work = kernel_work(Bl, S, d)
+        dom = max(k_ms, key=k_ms.get)                # dominant kernel on this rank
+        traffic = read_traffic(dom, args.config)
+        if traffic is not None:
+            traffic *= Bl / CONFIGS[args.config]["B"]   # per launch of this rank's shard
+        if args.config in ("cfg1", "cfg2"):
+            achieved = work[dom]["bytes"] / (k_ms[dom] / 1e3) / 1e9
+            roof = {"bound": "hbm", "achieved": achieved, "peak": pk_["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / pk_["hbm_gbs"], "kernel": dom, "traffic": traffic,
+                    "algorithmic_bytes": work[dom]["bytes"], "peak_source": pk_["source"]}
+        else:
+            achieved = work[dom]["flops"] / (k_ms[dom] / 1e3) / 1e12
+            sustained = ms_per_step > 100
+            pk_t = pk_["bf16_tflops_sustained"] if sustained else pk_["bf16_tflops"]
+            roof = {"bound": "tensor", "achieved": achieved, "peak": pk_t, "unit": "TFLOP/s",
+                    "frac": achieved / pk_t, "kernel": dom, "traffic": traffic,
+                    "algorithmic_flops": work[dom]["flops"],
+                    "peak_kind": "sustained (step > 100 ms)" if sustained else "burst",
+                    "peak_source": pk_["source"]}
 
     if rank != 0:
         if world > 1:
@@ -475,32 +567,33 @@ def main() -> int:
 
     cpu = None
     if not args.no_cpu_baseline and world == 1:
-        c = cpu_reference(cfg, args.config, steps=3, warmup=1, budget_s=20.0)
-        cpu = None if c is None else {k: c[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        c = cpu_reference(cfg, args.config, steps=3, warmup=1)
+        cpu = {k: c[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if "reference_layer" in c:
+            cpu["reference_layer"] = c["reference_layer"]
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate, fp32 in/out",
-        "data": "synthetic: x ~ N(0,1) fp32 seeded per rank, seeded default nn.Linear init, no mask",
-        "config": {"workload": args.config, **cfg, "causal": False, "per_gpu_batch": B,
-                   "global_batch": B * world, "parallelism": f"batch shards x{world} (no collective)",
+        "data": "synthetic: x ~ N(0,1) fp32 (sequence b drawn from a device generator seeded 101234+b), "
+                "seeded default nn.Linear init (seed 1234), no mask",
+        "config": {"workload": args.config, **cfg, "causal": False, "global_batch": B,
+                   "per_gpu_batch": -(-B // world),
+                   "parallelism": f"batch shards over {world} GPU(s), no data-path collective",
                    "l2": "inputs larger than L2" if T * d * 4 > L2_BYTES else "inputs smaller than L2 (no flush)"},
-        "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
-                "ms_per_step": e2e_ms, "path": "B200TransformerLayer.forward(pinned host x) -> host y, streamed in chunks with both copy directions overlapped"},
+        "e2e": e2e,
         "roofline": roof,
         "layer_roofline": {"hbm_gbs": bytes_layer / (ms_per_step / 1e3) / 1e9,
                            "hbm_frac": bytes_layer / (ms_per_step / 1e3) / 1e9 / pk_["hbm_gbs"],
                            "tflops": flops_layer / (ms_per_step / 1e3) / 1e12,
-                           "tflops_frac": flops_layer / (ms_per_step / 1e3) / 1e12 / pk_["bf16_tflops"]},
+                           "tflops_frac_sustained": flops_layer / (ms_per_step / 1e3) / 1e12
+                           / pk_["bf16_tflops_sustained"]},
         "kernel_ms": k_ms,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
-    if sharded is not None:
-        line["sharded_from_rank0"] = sharded
     print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

@@ -34,7 +34,27 @@ import torch.nn as nn
 from . import _lib
 
 GRAPH_MAX_INPUT_BYTES = 64 * 1024 * 1024   # reference gate, torch_transformer_benchmark.py:1077-1079
-HOST_CHUNK_BYTES = 16 * 1024 * 1024        # x bytes per chunk when streaming a host-resident batch
+HOST_CHUNK_BYTES = 16 * 1024 * 1024        # about this many x bytes per chunk when streaming a host batch
+
+
+def host_chunk_seqs(B: int, S: int, d: int, H: int, sms: int) -> int:
+    """Sequences per chunk when a host-resident batch streams through the GPU.
+
+    About HOST_CHUNK_BYTES of x per chunk, shaped so that each launch fills
+    the GPU: the whole-layer kernel (short sequences) walks sequence pairs,
+    one pair per SM at a time, so a chunk is a multiple of 2 x SMs sequences;
+    for longer sequences a chunk holds at least two sequences when the batch
+    has four or more, so the next chunk's copy overlaps a launch with enough
+    work items that its last wave is a small share."""
+    per_seq = max(1, S * d * 4)
+    if _lib.fused_shape(S, d, H):
+        unit = 2 * max(1, sms)
+        cb = unit * max(1, round(HOST_CHUNK_BYTES / (unit * per_seq)))
+    else:
+        cb = max(1, HOST_CHUNK_BYTES // per_seq)
+        if cb == 1 and B >= 4:
+            cb = 2
+    return max(1, min(B, cb))
 
 
 @dataclass(frozen=True)
@@ -108,6 +128,10 @@ class B200TransformerLayer(nn.Module):
     internal static buffer that the next call overwrites (as the reference's
     graph path returns, :1356-1360): copy it if it must outlive the next call.
     """
+
+    # forward(..., out=y) writes into a caller-provided tensor (used by the
+    # batch-sharded path to write each slice straight into its gather buffer).
+    accepts_out = True
 
     def __init__(self, d_model: int, num_heads: int, causal: bool = False, *,
                  use_graphs: bool = True) -> None:
@@ -234,11 +258,18 @@ class B200TransformerLayer(nn.Module):
                                      torch.cuda.current_stream(self._ws.device).cuda_stream)
         _lib.check(rc)
 
-    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None, *,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y = LN2(x + Attn(LN1(x))); ``out`` (optional, device x only): a
+        contiguous fp32 tensor of x's shape on x's device that receives y
+        (no CUDA-graph replay, no static buffer); it is returned."""
         if x.dim() != 3 or x.shape[-1] != self.attention.d_model:
             raise ValueError(f"expected x of shape [B, S, {self.attention.d_model}], got {tuple(x.shape)}")
         if x.dtype != torch.float32:
             raise TypeError(f"B200TransformerLayer computes fp32-in/fp32-out; got {x.dtype}")
+        if out is not None and (not x.is_cuda or out.device != x.device or out.shape != x.shape
+                                or out.dtype != torch.float32 or not out.is_contiguous()):
+            raise ValueError("out must be a contiguous fp32 tensor of x's shape on x's (CUDA) device")
         if not x.is_cuda:
             if self.norm1.weight.is_cuda:
                 # Host-resident input, parameters on the GPU: stream it through
@@ -266,9 +297,9 @@ class B200TransformerLayer(nn.Module):
                 self._graph = None
                 self._static_x = self._static_y = self._static_m = None
             small = x.numel() * x.element_size() <= GRAPH_MAX_INPUT_BYTES
-            if self.use_graphs and small:
+            if self.use_graphs and small and out is None:
                 return self._run_graphed(x, mask, pk)
-            y = torch.empty_like(x)
+            y = out if out is not None else torch.empty_like(x)
             self._launch(x, y, desc)
             return y
 
@@ -297,7 +328,7 @@ class B200TransformerLayer(nn.Module):
         """Host x -> host y through the GPU that holds the parameters.
 
         Sequences are independent (:1446-1447), so the batch moves in chunks
-        of about HOST_CHUNK_BYTES through a three-stream pipeline: host-to-
+        (``host_chunk_seqs``) through a three-stream pipeline: host-to-
         device copies on one stream, the layer on the caller's current stream,
         device-to-host copies on a third, with two device buffers for each of
         x and y. Both PCIe directions and the kernels overlap, so the call
@@ -313,7 +344,8 @@ class B200TransformerLayer(nn.Module):
                 raise ValueError(f"valid_token_mask must have shape {(B, S)}, got {tuple(valid_token_mask.shape)}")
             mask = valid_token_mask.to(torch.bool).contiguous().view(torch.uint8)
         x = x.contiguous()
-        cb = max(1, min(B, HOST_CHUNK_BYTES // max(1, S * d * 4)))
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        cb = host_chunk_seqs(B, S, d, self.attention.num_heads, sms)
         with torch.cuda.device(dev):
             pk = self._ensure_pack(dev)
             self._ensure_workspace(self._desc(cb, S, pk), dev)

@@ -12,9 +12,21 @@ rank so that a rank computes piece i while piece i+1 is still arriving.
 
 Weights are replicated: every rank builds or loads the same layer. With
 B < n only the first B ranks receive work; the rest still take part in the
-header broadcast and return at once. Head sharding (for B < n) is not
-offered: the out-projection mixes heads, so it would need an all-gather of
-ctx before the residual and LayerNorm.
+header broadcast and return at once (``head_sharded_forward`` in
+``headshard.py`` splits heads instead for that case).
+
+Host-resident input (the reference's ``_run_streamed``,
+torch_transformer_benchmark.py:1418-1508, spread over GPUs): with the NCCL
+backend, ``x`` on the source rank may be a CPU tensor (pinned, for
+asynchronous copies). The source then copies each piece host-to-device just
+before sending it -- the other ranks' pieces first, round-robin, so every rank
+starts computing as early as possible -- and copies each returned y piece
+device-to-host on a separate stream as soon as it lands, overlapped with its
+own compute. The result is a CPU tensor; both host copies run over the source
+GPU's own host link.
+
+Layers that accept ``out=`` (``B200TransformerLayer`` does) write each result
+straight into its place in the gathered output or in the send buffer.
 
 Failure behaviour: the caller's input is validated on ``src`` before any data
 moves and the verdict is broadcast, so a bad input raises the same
@@ -89,25 +101,38 @@ def _validate(x: Optional[torch.Tensor], mask: Optional[torch.Tensor]) -> int:
     return _HDR_OK
 
 
+def _run_into(layer, x: torch.Tensor, m: Optional[torch.Tensor], out: torch.Tensor) -> None:
+    """out <- layer(x, m), written in place when the layer supports ``out=``."""
+    if getattr(layer, "accepts_out", False):
+        layer(x, m, out=out)
+    else:
+        out.copy_(layer(x, m))
+
+
 def sharded_forward(layer: Callable[..., torch.Tensor], x: Optional[torch.Tensor] = None,
                     valid_token_mask: Optional[torch.Tensor] = None, *, src: int = 0,
                     group: Optional[dist.ProcessGroup] = None, device: Optional[torch.device] = None,
-                    chunks: int = 1) -> Optional[torch.Tensor]:
+                    chunks: int = 1, out: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """Run ``layer`` over the batch of ``x`` split across the ranks of ``group``.
 
-    Collective: every rank of ``group`` calls it; ``x`` (fp32 [B, S, d] on this
-    rank's device) and the optional ``valid_token_mask`` ([B, S] bool) are
-    read on ``src`` only. ``layer(x_slice, mask_slice)`` must map [b, S, d] to
-    [b, S, d] sequence by sequence (``B200TransformerLayer`` does). Returns y
-    [B, S, d] on ``src`` (the slices computed by the ranks, gathered into one
-    tensor) and ``None`` on every other rank.
+    Collective: every rank of ``group`` calls it; ``x`` (fp32 [B, S, d]) and
+    the optional ``valid_token_mask`` ([B, S] bool) are read on ``src`` only.
+    ``x`` lives on this rank's device, or -- with the NCCL backend -- on the
+    host (see the module docstring). ``layer(x_slice, mask_slice)`` must map
+    [b, S, d] to [b, S, d] sequence by sequence (``B200TransformerLayer``
+    does). Returns y [B, S, d] on ``src`` (the slices computed by the ranks,
+    gathered into one tensor on x's device, or into ``out`` when given) and
+    ``None`` on every other rank.
     """
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     src_g = dist.get_global_rank(group, src) if group is not None else src
     backend = dist.get_backend(group)
     if rank == src:
-        device = x.device if x is not None else (device or _default_device(backend))
+        if x is not None and x.device.type == "cpu" and backend == "nccl":
+            device = device or _default_device(backend)    # host input staged through this GPU
+        else:
+            device = x.device if x is not None else (device or _default_device(backend))
     elif device is None:
         device = _default_device(backend)
 
@@ -136,39 +161,97 @@ def sharded_forward(layer: Callable[..., torch.Tensor], x: Optional[torch.Tensor
     if saved_graphs:
         layer.use_graphs = False
     try:
-        return _exchange(layer, x, valid_token_mask, rank, world, src, src_g, group, device,
-                         B, S, d, has_mask, chunks)
+        if rank == src:
+            return _source(layer, x, valid_token_mask, world, src, group, device, B, has_mask, chunks, out)
+        return _exchange(layer, rank, world, src_g, group, device, B, S, d, has_mask, chunks)
     finally:
         if saved_graphs:
             layer.use_graphs = saved_graphs
 
 
-def _exchange(layer, x, valid_token_mask, rank, world, src, src_g, group, device, B, S, d, has_mask,
-              chunks):
+def _peer_pieces(shards, src, group, chunks):
+    """(global peer rank, c0, c1) of every piece that leaves the source, in
+    round-robin order over the peers, so each peer's first piece goes out
+    before any peer's second."""
+    per_peer = []
+    for r, (a, b) in enumerate(shards):
+        if r == src or a == b:
+            continue
+        peer = dist.get_global_rank(group, r) if group is not None else r
+        per_peer.append([(peer, c0, c1) for c0, c1 in _chunk_ranges(a, b, chunks)])
+    order = []
+    for i in range(max((len(p) for p in per_peer), default=0)):
+        order.extend(p[i] for p in per_peer if i < len(p))
+    return order
+
+
+def _source(layer, x, valid_token_mask, world, src, group, device, B, has_mask, chunks, out):
     shards = batch_shards(B, world)
+    pieces = _peer_pieces(shards, src, group, chunks)
+    host_io = x.device.type == "cpu" and device.type == "cuda"
+    x = x.contiguous()
+    mask = valid_token_mask.to(torch.uint8).contiguous() if has_mask else None
     works = []
-    if rank == src:
-        x = x.contiguous()
-        mask = valid_token_mask.to(torch.uint8).contiguous() if has_mask else None
-        y = torch.empty_like(x)
+    if not host_io:
+        y = out if out is not None else torch.empty_like(x)
         # Post every transfer first: x slices out, y slices back into y.
-        for r, (a, b) in enumerate(shards):
-            if r == src or a == b:
-                continue
-            peer = dist.get_global_rank(group, r) if group is not None else r
-            for c0, c1 in _chunk_ranges(a, b, chunks):
-                works.append(dist.isend(x[c0:c1], peer, group=group))
-                if mask is not None:
-                    works.append(dist.isend(mask[c0:c1], peer, group=group))
-            for c0, c1 in _chunk_ranges(a, b, chunks):
-                works.append(dist.irecv(y[c0:c1], peer, group=group))
+        for peer, c0, c1 in pieces:
+            works.append(dist.isend(x[c0:c1], peer, group=group))
+            if mask is not None:
+                works.append(dist.isend(mask[c0:c1], peer, group=group))
+        for peer, c0, c1 in pieces:
+            works.append(dist.irecv(y[c0:c1], peer, group=group))
         a, b = shards[src]
         for c0, c1 in _chunk_ranges(a, b, chunks):
             m = mask[c0:c1].bool() if mask is not None else None
-            y[c0:c1].copy_(layer(x[c0:c1], m))
+            _run_into(layer, x[c0:c1], m, y[c0:c1])
         for w in works:
             w.wait()
         return y
+
+    # Host input: stage through this GPU. Copies and NCCL transfers are
+    # ordered on the current stream (an NCCL send waits for the work queued on
+    # it), the returned pieces go device-to-host on a separate stream.
+    comp = torch.cuda.current_stream(device)
+    d2h = torch.cuda.Stream(device=device)
+    xd = torch.empty(x.shape, dtype=x.dtype, device=device)
+    yd = torch.empty_like(xd)
+    md = mask.to(device, non_blocking=True) if mask is not None else None
+    y = out if out is not None else torch.empty(x.shape, dtype=x.dtype, pin_memory=x.is_pinned())
+    for peer, c0, c1 in pieces:
+        xd[c0:c1].copy_(x[c0:c1], non_blocking=True)
+        works.append(dist.isend(xd[c0:c1], peer, group=group))
+        if md is not None:
+            works.append(dist.isend(md[c0:c1], peer, group=group))
+    recvs = [(dist.irecv(yd[c0:c1], peer, group=group), c0, c1) for peer, c0, c1 in pieces]
+    a, b = shards[src]
+    own = _chunk_ranges(a, b, chunks)
+    for c0, c1 in own:
+        xd[c0:c1].copy_(x[c0:c1], non_blocking=True)
+    # d2h_stream: each returned piece goes to the host once it has landed.
+    with torch.cuda.stream(d2h):
+        for w, c0, c1 in recvs:
+            w.wait()
+            y[c0:c1].copy_(yd[c0:c1], non_blocking=True)
+    for c0, c1 in own:
+        m = md[c0:c1].bool() if md is not None else None
+        _run_into(layer, xd[c0:c1], m, yd[c0:c1])
+    d2h.wait_stream(comp)
+    with torch.cuda.stream(d2h):
+        for c0, c1 in own:
+            y[c0:c1].copy_(yd[c0:c1], non_blocking=True)
+    for w in works:
+        w.wait()
+    comp.wait_stream(d2h)
+    xd.record_stream(d2h)
+    yd.record_stream(d2h)
+    comp.synchronize()     # y is complete on the host
+    return y
+
+
+def _exchange(layer, rank, world, src_g, group, device, B, S, d, has_mask, chunks):
+    shards = batch_shards(B, world)
+    works = []
 
     a, b = shards[rank]
     if a == b:
@@ -186,9 +269,9 @@ def _exchange(layer, x, valid_token_mask, rank, world, src, src_g, group, device
         if wm is not None:
             wm.wait()
         m = ms[c0:c1].bool() if ms is not None else None
-        # Copy out of the layer's result: it may be a static buffer that the
-        # next call overwrites while the send is still reading it.
-        ys[c0:c1].copy_(layer(xs[c0:c1], m))
+        # Into the send buffer (never the layer's static output buffer, which
+        # the next call would overwrite while the send still reads it).
+        _run_into(layer, xs[c0:c1], m, ys[c0:c1])
         works.append(dist.isend(ys[c0:c1], src_g, group=group))
     for w in works:
         w.wait()
@@ -199,7 +282,10 @@ class ShardedLayer(torch.nn.Module):
     """``forward(x, valid_token_mask=None)`` of a replicated layer, sharded by batch.
 
     Wraps a layer (every rank holds the same weights) so that the caller's
-    rank sees the reference module's API; see ``sharded_forward``."""
+    rank sees the reference module's API; see ``sharded_forward``. For a
+    host-resident x the result is a pinned host buffer owned by this module
+    and overwritten by the next host call of the same shape (as the layer's
+    own host path returns)."""
 
     def __init__(self, layer: torch.nn.Module, *, src: int = 0,
                  group: Optional[dist.ProcessGroup] = None, chunks: int = 1) -> None:
@@ -208,8 +294,15 @@ class ShardedLayer(torch.nn.Module):
         self.src = src
         self.group = group
         self.chunks = chunks
+        self._host_out: Optional[torch.Tensor] = None
 
     def forward(self, x: Optional[torch.Tensor] = None,
                 valid_token_mask: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+        out = None
+        if x is not None and x.device.type == "cpu" and dist.get_backend(self.group) == "nccl":
+            if self._host_out is None or self._host_out.shape != x.shape:
+                self._host_out = None
+                self._host_out = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
+            out = self._host_out
         return sharded_forward(self.layer, x, valid_token_mask, src=self.src, group=self.group,
-                               chunks=self.chunks)
+                               chunks=self.chunks, out=out)

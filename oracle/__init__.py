@@ -24,5 +24,8 @@ from .ref_layer import (  # noqa: F401
     generate_random_case,
     streamed_layer_rows_fp64,
     streamed_attention_rows_fp64,
+    streamed_keys,
+    streamed_ctx_rows,
+    streamed_output_rows,
 )
 from .compare import AccuracyResult, compare_outputs  # noqa: F401

@@ -216,26 +216,36 @@ def _ln64(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float) -> torc
     return (x - mean) / torch.sqrt(var + eps) * w + b
 
 
-def _attn_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor, rows: torch.Tensor,
-                    causal: bool) -> torch.Tensor:
-    """ctx rows [R, d] in fp64 for one sequence ``xs`` [S, d].
-
-    Follows ``chunked_attention`` (tools/reference_chunked.py:73-128): the
-    projections are done once over the whole sequence, then each head's
-    scores are formed for a block of queries against all keys (the key axis
-    is never blocked, so the softmax normalisation is exact), causal keys are
-    masked with -inf before the softmax (:109-113), and ctx = probs @ v (:120).
-    Only the sampled query rows are formed, so memory is O(R * S) per head.
-    """
+def streamed_keys(layer: ReferenceLayer, xs: torch.Tensor, dtype: torch.dtype = torch.float64):
+    """First phase of the streamed layer for one sequence ``xs`` [S, d]:
+    h = LN1(x) for every token and the K / V projections of every key
+    (tools/reference_chunked.py:73-128 projects the whole sequence once).
+    Returns (h, k, v) in ``dtype``."""
     att = layer.attention
-    H, dh = att.num_heads, att.head_dim
-    f = lambda t: t.detach().to(torch.float64)
+    f = lambda t: t.detach().to(dtype)
     h = _ln64(f(xs), f(layer.norm1.weight), f(layer.norm1.bias), layer.norm1.eps)
     k = h @ f(att.k_proj.weight).T + f(att.k_proj.bias)
     v = h @ f(att.v_proj.weight).T + f(att.v_proj.bias)
+    return h, k, v
+
+
+def streamed_ctx_rows(layer: ReferenceLayer, h: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      rows: torch.Tensor, causal: bool) -> torch.Tensor:
+    """Second phase: ctx rows [R, d] for the query positions ``rows``.
+
+    Follows ``chunked_attention`` (tools/reference_chunked.py:73-128): each
+    head's scores are formed for a block of queries against all keys (the key
+    axis is never blocked, so the softmax normalisation is exact), causal
+    keys are masked with -inf before the softmax (:109-113), and
+    ctx = probs @ v (:120). Only the sampled query rows are formed, so memory
+    is O(R * S) per head. Computed in the dtype of h / k / v.
+    """
+    att = layer.attention
+    H, dh = att.num_heads, att.head_dim
+    f = lambda t: t.detach().to(h.dtype)
     q = h[rows] @ f(att.q_proj.weight).T + f(att.q_proj.bias)
-    S = xs.shape[0]
-    ctx = torch.empty(rows.numel(), att.d_model, dtype=torch.float64)
+    S = h.shape[0]
+    ctx = torch.empty(rows.numel(), att.d_model, dtype=h.dtype)
     scale = dh ** -0.5
     for hh in range(H):
         sl = slice(hh * dh, (hh + 1) * dh)
@@ -247,6 +257,23 @@ def _attn_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor, rows: torch.Tensor,
         ctx[:, sl] = p @ v[:, sl]
         del sc, p
     return ctx
+
+
+def streamed_output_rows(layer: ReferenceLayer, xs: torch.Tensor, ctx: torch.Tensor,
+                         rows: torch.Tensor) -> torch.Tensor:
+    """Last phase: y rows = LN2(x + ctx Wo^T + bo) (:119, :141, :131), in ctx's dtype."""
+    att = layer.attention
+    f = lambda t: t.detach().to(ctx.dtype)
+    r = f(xs[rows]) + ctx @ f(att.out_proj.weight).T + f(att.out_proj.bias)
+    return _ln64(r, f(layer.norm2.weight), f(layer.norm2.bias), layer.norm2.eps)
+
+
+def _attn_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor, rows: torch.Tensor,
+                    causal: bool) -> torch.Tensor:
+    """ctx rows [R, d] in fp64 for one sequence ``xs`` [S, d] (streamed_keys,
+    then streamed_ctx_rows)."""
+    h, k, v = streamed_keys(layer, xs, torch.float64)
+    return streamed_ctx_rows(layer, h, k, v, rows, causal)
 
 
 def streamed_attention_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor,
@@ -265,11 +292,8 @@ def streamed_layer_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor,
     infeasible at S=100000, so the layer is restated per sampled row in fp64.
     """
     rows_t = torch.as_tensor(rows, dtype=torch.long)
-    att = layer.attention
-    f = lambda t: t.detach().to(torch.float64)
     ctx = _attn_rows_fp64(layer, xs, rows_t, causal)
-    r = f(xs[rows_t]) + ctx @ f(att.out_proj.weight).T + f(att.out_proj.bias)
-    return _ln64(r, f(layer.norm2.weight), f(layer.norm2.bias), layer.norm2.eps)
+    return streamed_output_rows(layer, xs, ctx, rows_t)
 
 
 def sample_rows(seq_len: int, count: int, seed: int) -> torch.Tensor:
@@ -297,6 +321,7 @@ def layer_bytes(batch: int, seq_len: int, d_model: int) -> float:
 __all__ = [
     "TransformerConfig", "ReferenceSelfAttention", "ReferenceLayer",
     "build_reference_layer", "generate_random_case", "streamed_layer_rows_fp64",
-    "streamed_attention_rows_fp64", "sample_rows", "layer_flops", "layer_bytes",
+    "streamed_attention_rows_fp64", "streamed_keys", "streamed_ctx_rows", "streamed_output_rows",
+    "sample_rows", "layer_flops", "layer_bytes",
 ]
 

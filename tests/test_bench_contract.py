@@ -31,6 +31,21 @@ def test_reference_arm_json_line():
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
 
 
-def test_reference_arm_marks_cfg5_infeasible():
+def test_reference_arm_cfg5_times_the_streamed_formulation():
+    """cfg5: the reference layer itself is infeasible ([B,H,S,S] scores), so
+    the arm times the reference's streamed formulation and says so."""
     d = _run("--impl", "reference", "--config", "cfg5", "--steps", "1", "--warmup", "1")
-    assert d["impl"] == "reference" and "unavailable" in d and "infeasible" in d["unavailable"]
+    assert d["impl"] == "reference" and d["value"] > 0
+    assert "infeasible" in d["reference_layer"]
+    assert "reference_chunked" in d["cpu_baseline"]["sample"]
+    assert d["config"]["workload"] == "cfg5"
+
+
+def test_default_workload_is_cfg5():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    assert m.DEFAULT_CONFIG == "cfg5"
+    assert m.shard_pieces(4, 100000, 1024) == 16
+    assert m.shard_pieces(1250, 128, 128) == 4

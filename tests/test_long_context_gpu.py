@@ -4,15 +4,20 @@ The reference cannot run this shape (its [B,H,S,S] scores would be 19,073 GiB,
 torch_transformer_benchmark.py:98), so correctness is checked as BASELINE.json
 prescribes: a seeded subset of 256 query positions per sequence against an fp64
 CPU oracle that streams over all keys (oracle.streamed_layer_rows_fp64, a
-restatement of tools/reference_chunked.py:73-128). Sequences are independent
-(:1446-1447), so 2 of cfg5's 32 sequences are run at full S.
+restatement of tools/reference_chunked.py:73-128). The full cfg5 batch of 32
+sequences runs in one launch (the launch the benchmark times: 32 x 16 x 391
+work items in the attention kernel's persistent scheduler), with sequences
+0, 15 and 31 checked; a batch of 2 covers the causal variant.
 """
+
+import os
 
 import pytest
 import torch
 
 from oracle import (TransformerConfig, build_reference_layer, compare_outputs,
-                    generate_random_case, streamed_attention_rows_fp64, streamed_layer_rows_fp64)
+                    generate_random_case, streamed_attention_rows_fp64, streamed_ctx_rows,
+                    streamed_keys, streamed_layer_rows_fp64, streamed_output_rows)
 from oracle.ref_layer import sample_rows
 from tests.test_layer_gpu import ws_views
 
@@ -45,4 +50,39 @@ def test_cfg5_sampled_rows_fp64(pkg, cuda_ok, causal):
         # max error relative to the largest context value
         c_ref = streamed_attention_rows_fp64(ref, x[b], rows, causal)
         rel = (ctx[b, rows] - c_ref).abs().max() / c_ref.abs().max()
+        assert rel < 1e-2, f"sequence {b}: ctx max error {rel:.3e} of max |ctx|"
+
+
+def test_cfg5_full_batch_one_launch(pkg, cuda_ok):
+    """cfg5 exactly as benchmarked: B = 32 in one forward (x generated on the
+    device from a seeded generator; 13 GB in, 13 GB out, 33 GB of workspace)."""
+    B, S, d, H = 32, 100000, 1024, 16
+    cfg = TransformerConfig(B, S, d, H)
+    ref = build_reference_layer(cfg, 1234)
+    lay = pkg.B200TransformerLayer(d, H, use_graphs=False).cuda().eval()
+    lay.load_state_dict(ref.state_dict(), strict=True)
+    x, _ = generate_random_case(cfg, seed=4321, device="cuda")
+    checked = (0, 15, 31)
+    with torch.inference_mode():
+        y = lay(x)
+        torch.cuda.synchronize()
+        lay.check_status()
+        _, _, _, ctx, _, _ = ws_views(pkg, lay, B, S, d, H)
+        ctx = ctx.view(B, S, d)
+        rows = {b: sample_rows(S, 256, seed=2000 + b) for b in checked}
+        xs = {b: x[b].cpu() for b in checked}
+        ys = {b: y[b, rows[b].cuda()].cpu() for b in checked}
+        cs = {b: ctx[b, rows[b].cuda()].cpu().double() for b in checked}
+    del x, y
+    torch.cuda.empty_cache()
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    for b in checked:
+        # the fp64 streamed oracle, keys projected once for both checks
+        h, k, v = streamed_keys(ref, xs[b], torch.float64)
+        c_ref = streamed_ctx_rows(ref, h, k, v, rows[b], False)
+        y_ref = streamed_output_rows(ref, xs[b], c_ref, rows[b])
+        del h, k, v
+        res = compare_outputs(y_ref, ys[b])
+        assert res.passed, f"sequence {b}: {res}"
+        rel = (cs[b] - c_ref).abs().max() / c_ref.abs().max()
         assert rel < 1e-2, f"sequence {b}: ctx max error {rel:.3e} of max |ctx|"

@@ -1,0 +1,82 @@
+"""Precision tail campaign on the GPU: many seeds, input scales and paddings.
+
+The reference's own campaign (tools/precision_probe.py:23-58, reported in
+report/TECH_REPORT.md:515-522) runs its optimized model against
+BaselineTransformer over seeds 1000+t, input scales 0.5 / 1 / 2 and padding
+ratios 0 / 0.3, and reports the worst max_abs error with its margin to the
+gate (atol / worst). This test does the same for BASELINE cfg1-cfg4 with the
+CPU fp32 oracle (pinned bit-exactly to the reference): 20 seeds x 3 scales x 2
+paddings = 120 cases per config, every output element under the reference's
+gate ``abs <= 2e-3 OR rel <= 2e-2``. cfg2's 10000 sequences are represented
+by a batch of 296 at full S (two sequences per SM on all 148 SMs), as the
+reference's sweep runs a batch subset at full S (tools/sweep.py:62-67);
+sequences are independent (torch_transformer_benchmark.py:1446-1447).
+
+Set B200L_TAIL_REPORT=<path> to write the per-config summary as JSON.
+"""
+
+import json
+import os
+
+import pytest
+import torch
+
+from oracle import TransformerConfig, build_reference_layer, compare_outputs, generate_random_case
+from oracle.compare import ATOL, RTOL
+
+pytestmark = pytest.mark.gpu
+
+SEEDS = range(1000, 1020)
+SCALES = (0.5, 1.0, 2.0)
+PADS = (0.0, 0.3)
+CONFIGS = {
+    "cfg1": (4, 128, 128, 4),
+    "cfg2": (296, 128, 128, 4),     # batch subset of cfg2's 10000, full S
+    "cfg3": (64, 128, 1024, 4),
+    "cfg4": (64, 1024, 128, 4),
+}
+_SUMMARY = {}
+
+
+def _gate_ratio(y_ref: torch.Tensor, y: torch.Tensor) -> float:
+    """Largest per-element min(err / atol, err / (rtol * |ref|)): an element
+    passes the OR gate exactly when its ratio is <= 1."""
+    r = y_ref.double()
+    err = (y.double() - r).abs()
+    ratio = torch.minimum(err / ATOL, err / (RTOL * r.abs()).clamp_min(1e-300))
+    return float(ratio.max())
+
+
+@pytest.mark.parametrize("name", sorted(CONFIGS))
+def test_precision_tail(pkg, cuda_ok, name):
+    B, S, d, H = CONFIGS[name]
+    cfg = TransformerConfig(B, S, d, H)
+    ref = build_reference_layer(cfg, 1234)
+    lay = pkg.B200TransformerLayer(d, H, use_graphs=False).cuda().eval()
+    lay.load_state_dict(ref.state_dict(), strict=True)
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    worst_abs, worst_ratio, failures, n = 0.0, 0.0, [], 0
+    with torch.inference_mode():
+        for scale in SCALES:
+            for pad in PADS:
+                for seed in SEEDS:
+                    x, mask = generate_random_case(cfg, seed=seed, padding_ratio=pad, input_scale=scale)
+                    m = mask if pad > 0 else None
+                    y = lay(x.cuda(), m.cuda() if m is not None else None).cpu()
+                    y_ref = ref(x, m)
+                    res = compare_outputs(y_ref, y)
+                    n += 1
+                    worst_abs = max(worst_abs, res.max_abs_error)
+                    worst_ratio = max(worst_ratio, _gate_ratio(y_ref, y))
+                    if not res.passed:
+                        failures.append((seed, scale, pad, res.failed_elements, res.max_abs_error))
+        torch.cuda.synchronize()
+        lay.check_status()
+    _SUMMARY[name] = {"B": B, "S": S, "d": d, "H": H, "cases": n, "worst_max_abs": worst_abs,
+                      "margin_atol_over_worst": ATOL / worst_abs if worst_abs > 0 else None,
+                      "worst_gate_ratio": worst_ratio, "failed_cases": len(failures)}
+    out = os.environ.get("B200L_TAIL_REPORT")
+    if out:
+        with open(out, "w") as f:
+            json.dump(_SUMMARY, f, indent=1)
+    assert not failures, f"{name}: {len(failures)} of {n} cases failed the gate, first {failures[:5]}"
