@@ -1,27 +1,35 @@
 // attn2.cuh -- K2 for head_dim <= 64: flash attention with two query tiles
-// per CTA and P kept in tensor memory.
+// per CTA, three MMA-issuing warps, and S, P and O in tensor memory.
 //
 // Same arithmetic as attn.cuh (BaselineSelfAttention.forward,
 // torch_transformer_benchmark.py:98-113, without materialising the scores);
 // the schedule is built for the long-sequence configs (S up to 100000,
-// head_dim 32 / 64), where the exponentials, not the tensor core, set the pace:
+// head_dim 32 / 64), where a single thread cannot issue tcgen05.mma fast
+// enough: measured on B200, one thread issues one M=128 MMA per 77-100
+// cycles whatever N (<= 128), while the tensor core finishes N=128 in ~64
+// cycles and N=64 in less; two threads issuing into different accumulators
+// reach the tensor core's own rate. So:
 //   * a work item is (b, h, 256 queries) = two 128-row query tiles that share
-//     every K / v^T tile (one TMA load feeds two S MMAs);
-//   * two softmax warpgroups, one per query tile, so one tile's softmax runs
-//     while the tensor core computes the other tile's S and P v;
-//   * S lands in one of three 128-column TMEM buffers used round-robin by the
-//     two tiles; the softmax writes P (fp16 pairs) over the S it has read, and
-//     tcgen05.mma reads P from TMEM as its A operand, so P never touches shared
-//     memory. A buffer is reused for the S three allocations later, which the
-//     MMA issuer enqueues only after the P v that reads the buffer, so the
-//     exponentials never wait for a P v to finish (only an O rescale does);
+//     every K / v^T tile (one TMA load feeds both tiles' MMAs);
+//   * three MMA-issuing threads: warp 1 issues S = Q K^T for both tiles, warps
+//     2 and 3 issue P v for tile 0 and 1; each query tile has its own softmax
+//     warpgroup (warps 4-7, 8-11), so the two tiles run as independent
+//     pipelines that only share the K / v^T ring;
+//   * per tile, TMEM holds S (fp32, 128 columns), P (fp16 pairs, 64 columns)
+//     and O (fp32, dhp columns): the softmax releases S as soon as the score
+//     row is in registers, so the next tile's S = Q K^T is computed while the
+//     exponentials of this one run; P waits in registers until the previous
+//     P v has read the P buffer, and tcgen05.mma reads P from TMEM as its A
+//     operand (P never touches shared memory);
 //   * K / v^T stream through a 3-stage TMA ring; lazy rescaling of O (only when
 //     a row max grows by more than 2^8).
-// TMEM (512 columns): S/P buffers [0,128) [128,256) [256,384),
-// O0 [384, 384+dhp) O1 [384+dhp, 384+2*dhp).
-// MMA order per key tile j: S_0(j), P_0 v(j-1), S_1(j), P_1 v(j-1).
-// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 4-7 softmax of tile 0,
-// 8-11 softmax of tile 1 (one query row per thread).
+// TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
+// O0 [384, 384+dhp) O1 [448, 448+dhp).
+// S issuer, per key tile j and tile t: S_t(j) once softmax t has read
+// S_t(j-1) (and K tile j has landed). P v issuer t: P_t(j) v_j once softmax t
+// has written P_t(j).
+// Warps: 0 TMA producer, 1 S issuer (owns TMEM), 2 / 3 P v issuers of tile
+// 0 / 1, 4-7 softmax of tile 0, 8-11 softmax of tile 1 (one query row per thread).
 #pragma once
 
 #include "attn.cuh"
@@ -39,8 +47,9 @@ struct Attn2Cfg {
   static constexpr int V_BYTES = DHP * BN * 2;         // v^T tile: DHP rows x 128 keys
   static constexpr int KVST = 3;
   static constexpr int SMEM = 2 * Q_BYTES + KVST * (K_BYTES + V_BYTES) + 256 + 1024;
-  static constexpr int NSB = 3;                        // S/P buffers of 128 columns
-  static constexpr int O_COL = 384;
+  static constexpr int S_COL = 0;      // + 128 * t
+  static constexpr int P_COL = 256;    // + 64 * t
+  static constexpr int O_COL = 384;    // + 64 * t
 };
 
 template <int DHP, bool KMASK>   // KMASK: a key-padding mask may be given
@@ -56,12 +65,13 @@ __global__ void __launch_bounds__(384, 1)
   uint8_t* sV = sK + C::KVST * C::K_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + C::KVST * C::V_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* q_empty = bars + 1;
+  uint64_t* q_empty = bars + 1;    // the S issuer releases Q after the item's last S
   uint64_t* kv_full = bars + 2;    // [3]
-  uint64_t* kv_empty = bars + 5;   // [3]
-  uint64_t* s_full = bars + 8;     // [3] one per S/P buffer
-  uint64_t* p_full = bars + 12;    // [2] one per query tile
-  uint64_t* pv_done = bars + 14;   // [2]
+  uint64_t* kv_empty = bars + 5;   // [3] both P v issuers release a stage after their P v of it
+  uint64_t* s_full = bars + 8;     // [2] per tile: S_t in TMEM
+  uint64_t* s_free = bars + 10;    // [2] per tile: the softmax warps have read S_t
+  uint64_t* p_full = bars + 12;    // [2] per tile: P_t written to TMEM
+  uint64_t* pv_done = bars + 14;   // [2] per tile: P_t v complete (P_t and O_t free)
   uint64_t* mma_done = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 18);   // bars 18-19
@@ -77,14 +87,15 @@ __global__ void __launch_bounds__(384, 1)
     mbar_init(q_empty, 1);
     for (int i = 0; i < 3; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);
     }
-    for (int b = 0; b < C::NSB; ++b) mbar_init(&s_full[b], 1);
     for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_free[t], 4);
       mbar_init(&p_full[t], 4);
       mbar_init(&pv_done[t], 1);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 3);
     waitctl_init(wc, status);
     fence_barrier_init();
     tma_prefetch_desc(&map_q);
@@ -126,7 +137,7 @@ __global__ void __launch_bounds__(384, 1)
           const int st = g % C::KVST;
           if (!mbar_wait(&kv_empty[st], ((g / C::KVST) & 1) ^ 1, wc)) { ok = false; break; }
           // Test hook: CTA 0 leaves out its first K / v^T load (nothing issued,
-          // so nothing to drain); the MMA issuer's bounded wait runs out.
+          // so nothing to drain); the MMA issuers' bounded waits run out.
           if (g == 0 && blockIdx.x == 0 && wc->site == kSiteAttnKv) continue;
           mbar_arrive_expect_tx(&kv_full[st], C::K_BYTES + C::V_BYTES);
           for (int kc = 0; kc < C::QKC; ++kc)
@@ -141,64 +152,83 @@ __global__ void __launch_bounds__(384, 1)
         if (lastkv[i] >= 0) mbar_drain(&kv_full[i], (lastkv[i] / C::KVST) & 1);
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // ================= MMA issuer
+    if (lane == 0) {  // ================= S issuer: S_t(j) = Q_t K_j^T for both tiles
       const uint32_t idesc_s = idesc_f16_f32(128, BN);
-      const uint32_t idesc_o = idesc_f16_f32(128, DHP);
-      // Shared-memory descriptors of the first Q / K / v^T tiles; every other
+      // Shared-memory descriptors of Q0 and of the first K stage; every other
       // operand is a fixed byte offset away, added to the start-address field
-      // (addresses stay below 256 KB, so the 14-bit field never carries).
+      // (addresses stay below 256 KB, so it never carries).
       const uint64_t dq0 = sdesc_kmajor(smem_u32(sQ), C::QKROW);
       const uint64_t dk0 = sdesc_kmajor(smem_u32(sK), C::QKROW);
-      const uint64_t dv0 = sdesc_kmajor(smem_u32(sV), 128);
-      // a: S allocations so far (buffer a % 3); g: key tiles so far (ring stage);
-      // np[t]: P v steps of tile t so far (p_full / pv_done phases).
-      int a = 0, g = 0, it = 0, np[2] = {0, 0};
+      // g: key tiles so far (ring stage); ns[t]: S steps of tile t so far.
+      int g = 0, it = 0, ns[2] = {0, 0};
       bool ok = true;
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x, ++it) {
         const int nqt = item_nqt(item);
         const int nkv = item_nkv(item);
         if (!mbar_wait(q_full, it & 1, wc)) break;
-        for (int j = 0; j <= nkv && ok; ++j) {
+        for (int j = 0; j < nkv && ok; ++j) {
           const int st = (g + j) % C::KVST;
-          if (j < nkv && !mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, wc)) { ok = false; break; }
+          if (!mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, wc)) { ok = false; break; }
+          const uint64_t dk = dk0 + (uint64_t)((st * C::K_BYTES) >> 4);
           for (int t = 0; t < nqt; ++t) {
-            if (j < nkv) {  // S_t(j) = Q_t K_j^T into buffer a % 3. Its previous
-              // user, allocation a - 3, had its P v enqueued before this MMA.
-              const int n = a + j * nqt + t;
-              const uint64_t dq = dq0 + (uint64_t)((t * C::Q_BYTES) >> 4);
-              const uint64_t dk = dk0 + (uint64_t)((st * C::K_BYTES) >> 4);
-              const uint32_t d_s = tmem_base + (uint32_t)(n % C::NSB) * 128;
-              tc_fence_after();
+            // S_t is free once softmax t has read the previous S_t.
+            if (ns[t] > 0 && !mbar_wait(&s_free[t], (ns[t] - 1) & 1, wc)) { ok = false; break; }
+            const uint64_t dq = dq0 + (uint64_t)((t * C::Q_BYTES) >> 4);
+            const uint32_t d_s = tmem_base + C::S_COL + t * 128;
+            tc_fence_after();
 #pragma unroll
-              for (int k = 0; k < DHP / 16; ++k) {
-                constexpr int R = C::QKROW;
-                const uint32_t off_q = (uint32_t)((k * 32) / R) * (128 * R) + (k * 32) % R;
-                const uint32_t off_k = (uint32_t)((k * 32) / R) * (BN * R) + (k * 32) % R;
-                umma_f16_ss(d_s, dq + (off_q >> 4), dk + (off_k >> 4), idesc_s, k > 0 ? 1u : 0u);
-              }
-              umma_commit(&s_full[n % C::NSB]);
-              if (j == nkv - 1 && t == nqt - 1) umma_commit(q_empty);
+            for (int k = 0; k < DHP / 16; ++k) {
+              constexpr int R = C::QKROW;
+              const uint32_t off_q = (uint32_t)((k * 32) / R) * (128 * R) + (k * 32) % R;
+              const uint32_t off_k = (uint32_t)((k * 32) / R) * (BN * R) + (k * 32) % R;
+              umma_f16_ss(d_s, dq + (off_q >> 4), dk + (off_k >> 4), idesc_s, k > 0 ? 1u : 0u);
             }
-            if (j > 0) {  // O_t += P_t(j-1) v_{j-1}, P from its S/P buffer in TMEM
-              const int n = a + (j - 1) * nqt + t;
-              const int stp = (g + j - 1) % C::KVST;
-              const uint64_t dv = dv0 + (uint64_t)((stp * C::V_BYTES) >> 4);
-              const uint32_t d_o = tmem_base + C::O_COL + t * DHP;
-              const uint32_t a_p = tmem_base + (uint32_t)(n % C::NSB) * 128;
-              const uint32_t acc0 = j > 1 ? 1u : 0u;
-              if (!mbar_wait(&p_full[t], np[t] & 1, wc)) { ok = false; break; }
-              tc_fence_after();
-#pragma unroll
-              for (int k = 0; k < BN / 16; ++k)
-                umma_f16_ts(d_o, a_p + k * 8, dv + ((uint32_t)((k >> 2) * (DHP * 128) + (k & 3) * 32) >> 4), idesc_o,
-                            k > 0 ? 1u : acc0);
-              umma_commit(&pv_done[t]);
-              ++np[t];
-              if (t == nqt - 1) umma_commit(&kv_empty[stp]);
-            }
+            umma_commit(&s_full[t]);
+            ++ns[t];
           }
         }
-        a += nqt * nkv;
+        if (ok) umma_commit(q_empty);   // after the item's last S: Q may be reloaded
+        g += nkv;
+      }
+      umma_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+  } else if (warp == 2 || warp == 3) {
+    if (lane == 0) {  // ================= P v issuer of query tile t: O_t += P_t(j) v_j
+      const int t = warp - 2;
+      const uint32_t idesc_o = idesc_f16_f32(128, DHP);
+      const uint64_t dv0 = sdesc_kmajor(smem_u32(sV), 128);
+      const uint32_t a_p = tmem_base + C::P_COL + t * 64;
+      const uint32_t d_o = tmem_base + C::O_COL + t * 64;
+      // g: key tiles so far (ring stage); np: P v steps of this tile so far.
+      int g = 0, np = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+        const int nqt = item_nqt(item);
+        const int nkv = item_nkv(item);
+        for (int j = 0; j < nkv && ok; ++j) {
+          const int st = (g + j) % C::KVST;
+          if (t >= nqt) {
+            // No second query tile in this item: release each K / v^T stage
+            // once it has landed (so this issuer never arrives on a stage
+            // ahead of the other one).
+            if (!mbar_wait(&kv_full[st], ((g + j) / C::KVST) & 1, wc)) { ok = false; break; }
+            umma_commit(&kv_empty[st]);
+            continue;
+          }
+          // P_t(j) in TMEM (softmax t read S_t(j), so K / v^T tile j has landed).
+          if (!mbar_wait(&p_full[t], np & 1, wc)) { ok = false; break; }
+          const uint64_t dv = dv0 + (uint64_t)((st * C::V_BYTES) >> 4);
+          const uint32_t acc0 = j > 0 ? 1u : 0u;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k)
+            umma_f16_ts(d_o, a_p + k * 8, dv + ((uint32_t)((k >> 2) * (DHP * 128) + (k & 3) * 32) >> 4), idesc_o,
+                        k > 0 ? 1u : acc0);
+          umma_commit(&pv_done[t]);
+          umma_commit(&kv_empty[st]);
+          ++np;
+        }
         g += nkv;
       }
       umma_commit(mma_done);
@@ -209,28 +239,25 @@ __global__ void __launch_bounds__(384, 1)
     const int qd = warp & 3;
     const int row = qd * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    const uint32_t t_o = tmem_base + lane_off + C::O_COL + t * DHP;
+    const uint32_t t_s = tmem_base + lane_off + C::S_COL + t * 128;
+    const uint32_t t_p = tmem_base + lane_off + C::P_COL + t * 64;
+    const uint32_t t_o = tmem_base + lane_off + C::O_COL + t * 64;
     const float sl2 = args.scale_log2;
-    int a = 0, np = 0;   // S allocations before this item; P v steps of tile t so far
+    int ns = 0, np = 0;   // S tiles read and P tiles written by this tile's softmax so far
     bool ok = true;
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
       const int nqt = item_nqt(item);
       const int nkv = item_nkv(item);
-      if (t >= nqt) {
-        a += nqt * nkv;
-        continue;
-      }
+      if (t >= nqt) continue;
       const int bh = item / QP;
       const int q0 = (item % QP) * 256 + t * 128;
       const int qpos = q0 + row;
       float m_use = 0.f, l = 0.f;
       const uint8_t* mrow = (KMASK && args.kmask) ? args.kmask + (long long)(bh / args.H) * S : nullptr;
-      for (int j = 0; j < nkv; ++j, ++np) {
-        const int n = a + j * nqt + t;
-        const uint32_t t_s = tmem_base + lane_off + (uint32_t)(n % C::NSB) * 128;
+      for (int j = 0; j < nkv; ++j) {
         uint32_t kb[BN / 32];
         if (KMASK && mrow) key_mask_load<BN / 32>(mrow, j * BN, S, lane, kb);
-        if (!mbar_wait_warp(&s_full[n % C::NSB], (n / C::NSB) & 1, wc)) { ok = false; break; }
+        if (!mbar_wait_warp(&s_full[t], ns & 1, wc)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
         {
@@ -239,6 +266,11 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(r[i]);
         }
+        // S_t is in registers: the issuer may compute the next S into it.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[t]);
+        ++ns;
 
         const int kv0 = j * BN;
         const bool need_mask = (kv0 + BN > S) || (args.causal && kv0 + BN - 1 > q0);
@@ -276,30 +308,28 @@ __global__ void __launch_bounds__(384, 1)
           m_use = m_cand;
           rescale = true;
         }
-        // p = 2^(s*scale*log2e - m), packed as fp16 pairs over the S just read.
-        // Pairs go through packed fp32x2 FMA/add, exponentials through MUFU.
+        // p = 2^(s*scale*log2e - m) as fp16 pairs, held in registers until the
+        // P buffer is free. Pairs go through packed fp32x2 FMA/add,
+        // exponentials through MUFU.
         const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_use, -m_use);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
+        uint32_t pk[BN / 2];
 #pragma unroll
-        for (int qq = 0; qq < 4; ++qq) {   // a quarter row (32 keys -> 16 fp16 pairs) at a time
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int e = 32 * qq + 2 * i;
-            const float2 xx = __ffma2_rn(make_float2(s[e], s[e + 1]), sc2, nm2);
-            const float2 pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
-            acc[i & 3] = __fadd2_rn(acc[i & 3], pp);
-            pk[i] = pack_half2(pp.x, pp.y);
-          }
-          tmem_st16_async(t_s + 16 * qq, pk);
+        for (int i = 0; i < BN / 2; ++i) {
+          const float2 xx = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
+          const float2 pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+          acc[i & 3] = __fadd2_rn(acc[i & 3], pp);
+          pk[i] = pack_half2(pp.x, pp.y);
         }
         const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
         l = l * alpha + ((a01.x + a01.y) + (a23.x + a23.y));
-        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-          // O_t is the previous P v's accumulator until that MMA completes.
+        // The previous P v must have read P_t and finished accumulating O_t.
+        if (np > 0) {
           if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
           tc_fence_after();
+        }
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int c = 0; c < DHP / 32; ++c) {
             uint32_t r[32];
@@ -309,13 +339,13 @@ __global__ void __launch_bounds__(384, 1)
             tmem_st32(t_o + c * 32, r);
           }
         }
-        tmem_wait_st();
+        tmem_st64(t_p, pk);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
+        ++np;
       }
       if (!ok) break;
-      a += nqt * nkv;
       // ---- epilogue: ctx row = O / l (fp16); rows beyond S are not stored.
       if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
       tc_fence_after();
