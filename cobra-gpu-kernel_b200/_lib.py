@@ -22,7 +22,7 @@ EXPORTED = (
     "b200l_kernel_workspace_bytes", "b200l_debug_arm", "b200l_noalloc_read_status",
 )
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # Fault-injection sites of b200l_debug_arm (test hook for the bounded waits).
 DEBUG_SITE_NONE = 0
@@ -52,7 +52,7 @@ class LayerDesc(ctypes.Structure):
         ("num_heads", c_int32), ("causal", c_int32), ("eps1", c_float), ("eps2", c_float),
         ("wqkv", c_void_p), ("bqkv", c_void_p), ("wo", c_void_p), ("bo", c_void_p),
         ("ln1_w", c_void_p), ("ln1_b", c_void_p), ("ln2_w", c_void_p), ("ln2_b", c_void_p),
-        ("valid_mask", c_void_p),
+        ("valid_mask", c_void_p), ("local_heads", c_int32),
     ]
 
 
@@ -143,7 +143,7 @@ def fused_shape(S: int, d: int, H: int) -> bool:
     return d in (64, 128) and d // H == 32 and d % H == 0 and S <= 128
 
 
-def workspace_layout(B: int, S: int, d: int, H: int) -> dict:
+def workspace_layout(B: int, S: int, d: int, H: int, local_heads: int = 0) -> dict:
     """Byte offsets of the workspace regions (mirror of ``make_plan`` in csrc/capi.cu).
 
     q, k: fp16 [B*H, S, dhp]; vt: fp16 [B*H, dhp, sp]; ctx: fp16 [B*S, d];
@@ -152,19 +152,20 @@ def workspace_layout(B: int, S: int, d: int, H: int) -> dict:
     b200l_layer_forward needs (the status block alone for the whole-layer
     kernel)."""
     dh = d // H
+    Hl = local_heads or H
     dhp = 32 if dh <= 32 else 64 if dh <= 64 else 128 if dh <= 128 else 256
     sp = _align(S, 8)
     T = B * S
     off = 1024
-    lay = {"dh": dh, "dhp": dhp, "sp": sp}
-    qk = B * H * S * dhp * 2
+    lay = {"dh": dh, "dhp": dhp, "sp": sp, "heads": Hl, "dq": Hl * dh}
+    qk = B * Hl * S * dhp * 2
     lay["q"] = off; off = _align(off + qk, 1024)
     lay["k"] = off; off = _align(off + qk, 1024)
-    lay["vt"] = off; off = _align(off + B * H * dhp * sp * 2, 1024)
-    lay["ctx"] = off; off = _align(off + T * d * 2, 1024)
+    lay["vt"] = off; off = _align(off + B * Hl * dhp * sp * 2, 1024)
+    lay["ctx"] = off; off = _align(off + T * Hl * dh * 2, 1024)
     lay["h"] = off
     if d > 256:
         off = _align(off + T * d * 2, 1024)
     lay["total"] = off
-    lay["layer_total"] = 1024 if fused_shape(S, d, H) else off
+    lay["layer_total"] = 1024 if (fused_shape(S, d, H) and Hl == H) else off
     return lay

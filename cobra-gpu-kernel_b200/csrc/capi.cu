@@ -145,6 +145,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct Plan {
   int B, S, d, H, dh, dhp, sp;
+  int Hl, dq;          // heads K1 / K2 compute (local_heads, or all H) and their width Hl * dh
   long long T;
   size_t off_q, off_k, off_vt, off_ctx, off_h;
   size_t total;        // status block + every intermediate: what K1 / K2 / K3 one at a time need
@@ -170,19 +171,23 @@ int make_plan(const b200l_layer_desc* desc, Plan* p) {
   const int sp = (S + 7) / 8 * 8;
   if ((long long)B * H * ((S + 127) / 128) > 0x7fffffffLL || T > 0x7fffffffLL)
     return fail(B200L_ERR_BAD_SHAPE, "problem too large for 32-bit tile indices");
+  if (desc->local_heads < 0 || desc->local_heads > H)
+    return fail(B200L_ERR_BAD_SHAPE, "local_heads %d must be in [0, num_heads = %d]", desc->local_heads, H);
+  const int Hl = desc->local_heads ? desc->local_heads : H;
   p->B = B; p->S = S; p->d = d; p->H = H; p->dh = dh; p->dhp = dhp; p->sp = sp; p->T = T;
+  p->Hl = Hl; p->dq = Hl * dh;
   size_t off = 1024;  // status block (256 B) padded to keep every region 1024-aligned
-  const size_t qk = (size_t)B * H * S * dhp * 2;
+  const size_t qk = (size_t)B * Hl * S * dhp * 2;
   p->off_q = off; off = align_up(off + qk, 1024);
   p->off_k = off; off = align_up(off + qk, 1024);
-  p->off_vt = off; off = align_up(off + (size_t)B * H * dhp * sp * 2, 1024);
-  p->off_ctx = off; off = align_up(off + (size_t)T * d * 2, 1024);
+  p->off_vt = off; off = align_up(off + (size_t)B * Hl * dhp * sp * 2, 1024);
+  p->off_ctx = off; off = align_up(off + (size_t)T * p->dq * 2, 1024);
   p->off_h = off;
   if (d > 256) off = align_up(off + (size_t)T * d * 2, 1024);
   p->total = off;
   // The whole-layer kernel keeps h, q, k, v and ctx on chip: it touches only
   // the status block.
-  p->fused = fused_shape(S, d, dh);
+  p->fused = fused_shape(S, d, dh) && Hl == H;
   p->layer_total = p->fused ? 1024 : p->total;
   return B200L_OK;
 }
@@ -215,7 +220,7 @@ QkvOut qkv_out(const Plan& p, void* ws) {
   o.q = reinterpret_cast<__half*>(w + p.off_q);
   o.k = reinterpret_cast<__half*>(w + p.off_k);
   o.vt = reinterpret_cast<__half*>(w + p.off_vt);
-  o.S = p.S; o.H = p.H; o.dh = p.dh; o.dhp = p.dhp; o.sp = p.sp; o.d = p.d;
+  o.S = p.S; o.H = p.Hl; o.dh = p.dh; o.dhp = p.dhp; o.sp = p.sp; o.dq = p.dq;
   return o;
 }
 
@@ -247,14 +252,14 @@ int launch_row_ln(const float* in, void* out, const float* w, const float* b, fl
 template <int KP>
 int launch_qkv_lnfused_t(const b200l_layer_desc* desc, const Plan& p, const float* x, void* ws, cudaStream_t st) {
   CUtensorMap map_w;
-  int rc = map_rows_k(&map_w, desc->wqkv, 3ull * p.d, p.d, 128, "wqkv");
+  int rc = map_rows_k(&map_w, desc->wqkv, 3ull * p.dq, p.d, 128, "wqkv");
   if (rc) return rc;
   auto kern = qkv_lnfused_kernel<KP>;
   const int smem = QkvLnFusedCfg<KP>::SMEM;
   if ((rc = ensure_smem((const void*)kern, smem))) return rc;
   const long long blocks = (p.T + 127) / 128;
   kern<<<(unsigned)blocks, 256, smem, st>>>(map_w, x, desc->ln1_w, desc->ln1_b, desc->eps1, desc->bqkv, qkv_out(p, ws),
-                                            p.T, p.d, reinterpret_cast<DevStatus*>(ws));
+                                            p.T, p.d, 3 * p.dq, reinterpret_cast<DevStatus*>(ws));
   return check_launch("qkv_lnfused_kernel");
 }
 
@@ -289,7 +294,7 @@ int run_qkv(const b200l_layer_desc* desc, const Plan& p, const float* x, void* w
   if (rc) return rc;
   CUtensorMap map_a, map_b;
   if ((rc = map_rows_k(&map_a, h, (unsigned long long)p.T, p.d, 128, "h"))) return rc;
-  if ((rc = map_rows_k(&map_b, desc->wqkv, 3ull * p.d, p.d, 256, "wqkv"))) return rc;
+  if ((rc = map_rows_k(&map_b, desc->wqkv, 3ull * p.dq, p.d, 256, "wqkv"))) return rc;
   EpiArgs ea{};
   ea.qkv = qkv_out(p, ws);
   ea.bias = desc->bqkv;
@@ -297,7 +302,7 @@ int run_qkv(const b200l_layer_desc* desc, const Plan& p, const float* x, void* w
   // Three stages (144 KB): the q / k / v^T scatter epilogue, not the operand
   // ring, bounds this GEMM (without its stores it ran 26 % faster), and with
   // four stages it measured 4 % slower.
-  return launch_gemm_tma_t<256, 3, EPI_QKV>(map_a, map_b, ea, p.T, p.d, 3 * p.d, ws, st);
+  return launch_gemm_tma_t<256, 3, EPI_QKV>(map_a, map_b, ea, p.T, p.d, 3 * p.dq, ws, st);
 }
 
 // TWO_TILE: the two-query-tile kernel with P in TMEM (head_dim <= 64);
@@ -305,7 +310,7 @@ int run_qkv(const b200l_layer_desc* desc, const Plan& p, const float* x, void* w
 template <int DHP, int BN, bool TWO_TILE = false>
 int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& dev, void* ws, cudaStream_t st) {
   uint8_t* w = static_cast<uint8_t*>(ws);
-  const unsigned long long BH = (unsigned long long)p.B * p.H;
+  const unsigned long long BH = (unsigned long long)p.B * p.Hl;
   CUtensorMap mq, mk, mv;
   const CUtensorMapSwizzle qk_swz = DHP >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const unsigned qk_inner = DHP >= 64 ? 64 : 32;
@@ -327,7 +332,7 @@ int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& de
   }
   AttnArgs a;
   a.ctx = reinterpret_cast<__half*>(w + p.off_ctx);
-  a.B = p.B; a.S = p.S; a.H = p.H; a.dh = p.dh; a.d = p.d;
+  a.B = p.B; a.S = p.S; a.H = p.Hl; a.dh = p.dh; a.d = p.dq;   // ctx rows hold the computed heads
   a.causal = desc->causal ? 1 : 0;
   a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)p.dh));
   a.num_items = (int)(BH * (unsigned long long)((p.S + 127) / 128));
@@ -622,6 +627,7 @@ int b200l_outproj_res_ln(const b200l_layer_desc* desc, const float* x, float* y,
   DevInfo dev;
   int rc = check_common(desc, workspace, ws_bytes, &p, &dev);
   if (rc) return rc;
+  if (p.Hl != p.H) return fail(B200L_ERR_BAD_SHAPE, "the out-projection needs every head's ctx: local_heads must be 0");
   if ((rc = check_xy(x, y, true))) return rc;
   return run_outproj(desc, p, x, y, workspace, static_cast<cudaStream_t>(stream));
 }
@@ -632,6 +638,7 @@ int b200l_layer_forward(const b200l_layer_desc* desc, const float* x, float* y, 
   DevInfo dev;
   int rc = check_common(desc, workspace, ws_bytes, &p, &dev, /*whole_layer=*/true);
   if (rc) return rc;
+  if (p.Hl != p.H) return fail(B200L_ERR_BAD_SHAPE, "b200l_layer_forward computes every head: local_heads must be 0");
   if ((rc = check_xy(x, y, true))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p.fused) return run_fused(desc, p, dev, x, y, workspace, st);
@@ -651,6 +658,7 @@ int b200l_block_forward(const b200l_block_desc* desc, const float* x, float* y, 
   BlockPlan bp;
   int rc = make_block_plan(desc, &bp);
   if (rc) return rc;
+  if (bp.p.Hl != bp.p.H) return fail(B200L_ERR_BAD_SHAPE, "b200l_block_forward computes every head: local_heads must be 0");
   if (!desc->w1 || !desc->b1 || !desc->w2 || !desc->b2) return fail(B200L_ERR_NULL_POINTER, "FFN weight is NULL");
   Plan p;
   DevInfo dev;

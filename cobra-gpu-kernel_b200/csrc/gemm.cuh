@@ -23,15 +23,16 @@ struct QkvOut {
   __half* q;
   __half* k;
   __half* vt;
-  int S, H, dh, dhp, sp, d;
+  int S, H, dh, dhp, sp;
+  int dq;   // width of each of the q / k / v projections: H * dh (the heads computed)
 };
 
 // Stores 32 consecutive projection columns [col0, col0+32) of token t.
 // dh is a multiple of 32, so the chunk lies inside one (q|k|v, head) block.
 __device__ __forceinline__ void qkv_store_chunk(const QkvOut& o, const float* __restrict__ bqkv, long long t,
                                                 int col0, const uint32_t (&acc)[32]) {
-  const int which = col0 / o.d;
-  const int within = col0 - which * o.d;
+  const int which = col0 / o.dq;
+  const int within = col0 - which * o.dq;
   const int head = within / o.dh;
   const int j0 = within - head * o.dh;
   const long long b = t / o.S;
@@ -95,7 +96,7 @@ template <int KP>
 __global__ void __launch_bounds__(256, 1)
     qkv_lnfused_kernel(const __grid_constant__ CUtensorMap map_w, const float* __restrict__ x,
                        const float* __restrict__ ln_w, const float* __restrict__ ln_b, float eps,
-                       const float* __restrict__ bqkv, QkvOut out, long long T, int d, DevStatus* status) {
+                       const float* __restrict__ bqkv, QkvOut out, long long T, int d, int N, DevStatus* status) {
   using C = QkvLnFusedCfg<KP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -112,8 +113,7 @@ __global__ void __launch_bounds__(256, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long m0 = (long long)blockIdx.x * 128;
-  const int N = 3 * d;
-  const int NT = (N + 127) / 128;
+  const int NT = (N + 127) / 128;   // N = 3 * out.dq projection columns
   const int KS = (d + 15) / 16;
 
   if (threadIdx.x == 0) {

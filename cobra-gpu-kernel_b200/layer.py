@@ -132,6 +132,8 @@ class B200TransformerLayer(nn.Module):
     # forward(..., out=y) writes into a caller-provided tensor (used by the
     # batch-sharded path to write each slice straight into its gather buffer).
     accepts_out = True
+    # dtype of the ctx columns _head_ctx returns (head sharding).
+    ctx_dtype = torch.float16
 
     def __init__(self, d_model: int, num_heads: int, causal: bool = False, *,
                  use_graphs: bool = True) -> None:
@@ -153,6 +155,8 @@ class B200TransformerLayer(nn.Module):
         self._host_out = None
         self._io_streams = None
         self._warm = set()
+        self._head_packs = {}
+        self._hws: Optional[torch.Tensor] = None
         self.register_load_state_dict_post_hook(lambda mod, _keys: mod.invalidate())
 
     @classmethod
@@ -165,6 +169,7 @@ class B200TransformerLayer(nn.Module):
     def invalidate(self) -> None:
         """Drop packed weights and captured graphs (weights changed)."""
         self._pack = None
+        self._head_packs = {}
         self._graph = None
         self._static_x = self._static_y = self._static_m = None
         self._sig = None
@@ -257,6 +262,79 @@ class B200TransformerLayer(nn.Module):
             rc = L.b200l_read_status(self.workspace_ptr,
                                      torch.cuda.current_stream(self._ws.device).cuda_stream)
         _lib.check(rc)
+
+    # ------------------------------------------------------------ head sharding
+    def _head_pack(self, device: torch.device, h0: int, h1: int):
+        """fp16 q|k|v weight rows and fp32 biases of heads [h0, h1) on ``device``."""
+        versions = self._param_versions()
+        key = (device, h0, h1)
+        hp = self._head_packs.get(key)
+        if hp is not None and hp[2] == versions:
+            return hp
+        att = self.attention
+        sl = slice(h0 * att.head_dim, h1 * att.head_dim)
+        w = torch.cat([m.weight[sl] for m in (att.q_proj, att.k_proj, att.v_proj)]).detach()
+        w = w.to(device=device, dtype=torch.float32).contiguous()
+        b = torch.cat([m.bias[sl] for m in (att.q_proj, att.k_proj, att.v_proj)]).detach()
+        b = b.to(device=device, dtype=torch.float32).contiguous()
+        w16 = torch.empty(w.shape, dtype=torch.float16, device=device)
+        with torch.cuda.device(device):
+            _lib.check(_lib.lib().b200l_cast_f16(w.data_ptr(), w16.data_ptr(), w.numel(),
+                                                 torch.cuda.current_stream(device).cuda_stream))
+        torch.cuda.current_stream(device).synchronize()   # w (fp32 staging) is read
+        hp = (w16, b, versions)
+        self._head_packs[key] = hp
+        return hp
+
+    def _head_ctx(self, x: torch.Tensor, mask: Optional[torch.Tensor], h0: int, h1: int) -> torch.Tensor:
+        """ctx columns of heads [h0, h1) for the whole batch, fp16 [B*S, (h1-h0)*d_h]:
+        K1 (LN1 + the q / k / v projections of those heads) and K2 through the
+        C ABI with ``local_heads`` (used by ``headshard.head_sharded_forward``)."""
+        B, S, _ = x.shape
+        dev = x.device
+        L = _lib.lib()
+        m8 = mask.to(torch.bool).contiguous().view(torch.uint8) if mask is not None else None
+        with torch.cuda.device(dev):
+            pk = self._ensure_pack(dev)
+            w16, b32, _ = self._head_pack(dev, h0, h1)
+            desc = self._desc(B, S, pk, m8)
+            desc.wqkv, desc.bqkv, desc.local_heads = w16.data_ptr(), b32.data_ptr(), h1 - h0
+            need = L.b200l_kernel_workspace_bytes(ctypes.byref(desc))
+            if need == 0:
+                raise _lib.B200LError(-1, _lib.last_error())
+            if self._hws is None or self._hws.device != dev or self._hws.numel() < need + 1024:
+                self._hws = None
+                self._hws = torch.zeros(need + 1024, dtype=torch.uint8, device=dev)
+            off = (-self._hws.data_ptr()) % 1024
+            ws = self._hws.data_ptr() + off
+            st = torch.cuda.current_stream(dev).cuda_stream
+            _lib.check(L.b200l_clear_status(ws, st))
+            _lib.check(L.b200l_qkv_ln_gemm(ctypes.byref(desc), x.data_ptr(), ws, need, st))
+            _lib.check(L.b200l_flash_attn(ctypes.byref(desc), ws, need, st))
+            _lib.check(L.b200l_read_status(ws, st))
+            lay = _lib.workspace_layout(B, S, self.attention.d_model, self.attention.num_heads, h1 - h0)
+            n = B * S * lay["dq"]
+            ctx = self._hws[off + lay["ctx"]:off + lay["ctx"] + 2 * n].view(torch.float16)
+            return ctx.view(B * S, lay["dq"]).clone()
+
+    def _finish_from_ctx(self, x: torch.Tensor, mask: Optional[torch.Tensor], ctx: torch.Tensor) -> torch.Tensor:
+        """y = LN2(x + ctx Wo^T + bo) from every head's ctx (fp16 [B*S, d]): K3
+        through the C ABI on this layer's own workspace."""
+        B, S, d = x.shape
+        dev = x.device
+        L = _lib.lib()
+        m8 = mask.to(torch.bool).contiguous().view(torch.uint8) if mask is not None else None
+        with torch.cuda.device(dev):
+            pk = self._ensure_pack(dev)
+            desc = self._desc(B, S, pk, m8)
+            self._ensure_workspace(desc, dev, stepwise=True)
+            lay = _lib.workspace_layout(B, S, d, self.attention.num_heads)
+            base = self._ws[self._ws_off + lay["ctx"]:self._ws_off + lay["ctx"] + 2 * B * S * d]
+            base.view(torch.float16).view(B * S, d).copy_(ctx)
+            y = torch.empty_like(x)
+            _lib.check(L.b200l_outproj_res_ln(ctypes.byref(desc), x.data_ptr(), y.data_ptr(), self.workspace_ptr,
+                                              self._ws_bytes, torch.cuda.current_stream(dev).cuda_stream))
+            return y
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None, *,
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define B200L_ABI_VERSION 3
+#define B200L_ABI_VERSION 4
 
 enum b200l_status {
     B200L_OK = 0,
@@ -91,6 +91,16 @@ typedef struct b200l_layer_desc {
      * (after the out-projection and its bias) is zeroed, so that row of y is
      * LN2(x). Read by the attention and out-projection kernels. */
     const uint8_t* valid_mask;
+    /* Head sharding (0 = every head, the normal case). When 0 < local_heads
+     * <= num_heads, K1 and K2 (b200l_qkv_ln_gemm, b200l_flash_attn) compute
+     * only local_heads heads: wqkv / bqkv hold those heads' rows (their q
+     * rows, then their k rows, then their v rows, each local_heads * dh), and
+     * ctx in the workspace is [T, local_heads * dh]. The out-projection mixes
+     * every head (torch_transformer_benchmark.py:119), so b200l_outproj_res_ln,
+     * b200l_layer_forward and b200l_block_forward need local_heads == 0: a
+     * head-sharded caller gathers every rank's ctx columns first (see
+     * headshard.py in the package). */
+    int32_t local_heads;
 } b200l_layer_desc;
 
 /* ABI version (B200L_ABI_VERSION). */

@@ -1,5 +1,8 @@
-"""Batch sharding over NCCL on two B200s: the gathered output is bitwise equal
-to the one-GPU output (every sequence runs the same kernels either way).
+"""Batch and head sharding over NCCL on two B200s: the gathered output is
+bitwise equal to the one-GPU output (every sequence runs the same kernels
+either way), also when x starts in rank 0's host memory; head sharding
+(ctx columns gathered from both ranks) equals the same head ranges computed
+on one GPU and passes the reference gate.
 
 Skipped unless two sm_100 devices are visible. Ranks are spawned processes,
 one per GPU, with a short process-group timeout.
@@ -64,6 +67,40 @@ def _worker(rank: int, world: int, port: int, root: str) -> None:
                     single = layer(x).clone()
                     torch.cuda.synchronize(dev)
                     assert torch.equal(y, single), f"case {(B, S, d, H, causal, chunks)}"
+                else:
+                    assert y is None
+            # Host-resident x on rank 0: pieces staged through rank 0's GPU.
+            cfg = TransformerConfig(6, 300, 256, 4)
+            ref = build_reference_layer(cfg, seed=23)
+            layer = pkg.B200TransformerLayer(256, 4).to(dev).eval()
+            layer.load_state_dict(ref.state_dict(), strict=True)
+            x, _ = generate_random_case(cfg, seed=24)
+            xh = x.pin_memory() if rank == 0 else None
+            y = pkg.ShardedLayer(layer, chunks=2)(xh)
+            torch.cuda.synchronize(dev)
+            layer.check_status()
+            if rank == 0:
+                assert y.device.type == "cpu"
+                single = layer(x.to(dev)).cpu()
+                assert torch.equal(y, single), "host-resident sharded output differs"
+            # Head sharding (B smaller than the number of ranks' work): cfg1 shape.
+            for B, S, d, H, pad in ((4, 128, 128, 4, 0.0), (2, 200, 256, 4, 0.3)):
+                cfg = TransformerConfig(B, S, d, H)
+                ref = build_reference_layer(cfg, seed=25)
+                layer = pkg.B200TransformerLayer(d, H).to(dev).eval()
+                layer.load_state_dict(ref.state_dict(), strict=True)
+                x, mask = generate_random_case(cfg, seed=26, padding_ratio=pad)
+                m = mask.to(dev) if pad > 0 else None
+                y = pkg.head_sharded_forward(layer, x.to(dev) if rank == 0 else None,
+                                             m if rank == 0 else None)
+                torch.cuda.synchronize(dev)
+                if rank == 0:
+                    from oracle import compare_outputs
+                    res = compare_outputs(ref(x, mask if pad > 0 else None), y.cpu())
+                    assert res.passed, f"head-sharded {(B, S, d, H)}: {res}"
+                    parts = [layer._head_ctx(x.to(dev), m, a, b) for a, b in pkg.head_shards(H, world)]
+                    single = layer._finish_from_ctx(x.to(dev), m, torch.cat(parts, 1))
+                    assert torch.equal(y, single), "head-sharded output differs from one GPU"
                 else:
                     assert y is None
         dist.barrier()
