@@ -20,7 +20,11 @@ EXPORTED = (
     "b200l_outproj_res_ln", "b200l_layer_forward_noalloc", "b200l_block_workspace_bytes",
     "b200l_block_forward", "b200l_row_layernorm", "b200l_cast_f16",
     "b200l_kernel_workspace_bytes", "b200l_debug_arm", "b200l_noalloc_read_status",
+    "b200l_convert",
 )
+
+# Element types of b200l_convert.
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 
 ABI_VERSION = 4
 
@@ -98,6 +102,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "b200l_kernel_workspace_bytes": (c_size_t, [P]),
         "b200l_debug_arm": (c_int, [P, c_int32, ctypes.c_uint64, P]),
         "b200l_noalloc_read_status": (c_int, [P]),
+        "b200l_convert": (c_int, [P, c_int32, P, c_int32, ctypes.c_int64, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -1,35 +1,46 @@
 // attn2.cuh -- K2 for head_dim <= 64: flash attention with two query tiles
-// per CTA, three MMA-issuing warps, and S, P and O in tensor memory.
+// per CTA, three MMA-issuing warps, sixteen softmax warps, and S, P and O in
+// tensor memory.
 //
 // Same arithmetic as attn.cuh (BaselineSelfAttention.forward,
 // torch_transformer_benchmark.py:98-113, without materialising the scores);
 // the schedule is built for the long-sequence configs (S up to 100000,
-// head_dim 32 / 64), where a single thread cannot issue tcgen05.mma fast
-// enough: measured on B200, one thread issues one M=128 MMA per 77-100
-// cycles whatever N (<= 128), while the tensor core finishes N=128 in ~64
-// cycles and N=64 in less; two threads issuing into different accumulators
-// reach the tensor core's own rate. So:
+// head_dim 32 / 64). Measured on B200 (one SM, clock64):
+//   * one thread issues one M=128 tcgen05.mma per 77-100 cycles whatever N
+//     (<= 128), while the tensor core finishes N=128 in ~64 cycles; two
+//     threads issuing into different accumulators reach the tensor core's
+//     own rate -- so the MMAs are spread over three issuing threads;
+//   * the exponentials (FFMA2 -> 2x MUFU ex2 -> FADD2 + fp16 pack per pair of
+//     scores) reach 74 % of MUFU throughput with one warp per scheduler, 90 %
+//     with two and 96 % with three or four -- so each 32-row quarter of a
+//     query tile is split over two warps by key halves, four softmax warps
+//     per scheduler;
+//   * under MUFU load every shared-memory / barrier / TMEM round trip of a
+//     warp costs 150-250 cycles, so each warp's step is a short fixed chain
+//     of them around its exponentials.
+// Structure:
 //   * a work item is (b, h, 256 queries) = two 128-row query tiles that share
 //     every K / v^T tile (one TMA load feeds both tiles' MMAs);
-//   * three MMA-issuing threads: warp 1 issues S = Q K^T for both tiles, warps
-//     2 and 3 issue P v for tile 0 and 1; each query tile has its own softmax
-//     warpgroup (warps 4-7, 8-11), so the two tiles run as independent
-//     pipelines that only share the K / v^T ring;
+//   * warp 1 issues S = Q K^T for both tiles, warps 2 and 3 issue P v for
+//     tile 0 and 1;
+//   * warps 4-19 are the softmax: warp 4 + 8t + 4c + q handles rows
+//     32q..32q+31 of tile t and keys [64c, 64c + 64) of every 128-key tile;
+//     the two warps of a row agree on the row maximum through shared memory
+//     and a 64-thread named barrier once per key tile, and add their row sums
+//     at the end of the item;
 //   * per tile, TMEM holds S (fp32, 128 columns), P (fp16 pairs, 64 columns)
-//     and O (fp32, dhp columns): the softmax releases S as soon as the score
-//     row is in registers, so the next tile's S = Q K^T is computed while the
-//     exponentials of this one run; P waits in registers until the previous
-//     P v has read the P buffer, and tcgen05.mma reads P from TMEM as its A
-//     operand (P never touches shared memory);
+//     and O (fp32, dhp columns): the softmax releases S as soon as its half
+//     row is in registers, so the next S = Q K^T is computed while the
+//     exponentials run; P waits in registers until the previous P v has read
+//     the P buffer, and tcgen05.mma reads P from TMEM as its A operand (P
+//     never touches shared memory);
 //   * K / v^T stream through a 3-stage TMA ring; lazy rescaling of O (only when
-//     a row max grows by more than 2^8).
+//     a row max grows by more than 2^8; each half rescales its half of O).
 // TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 // O0 [384, 384+dhp) O1 [448, 448+dhp).
-// S issuer, per key tile j and tile t: S_t(j) once softmax t has read
-// S_t(j-1) (and K tile j has landed). P v issuer t: P_t(j) v_j once softmax t
-// has written P_t(j).
-// Warps: 0 TMA producer, 1 S issuer (owns TMEM), 2 / 3 P v issuers of tile
-// 0 / 1, 4-7 softmax of tile 0, 8-11 softmax of tile 1 (one query row per thread).
+// S issuer, per key tile j and tile t: S_t(j) once both halves of softmax t
+// have read S_t(j-1) (and K tile j has landed). P v issuer t: P_t(j) v_j once
+// both halves have written P_t(j).
 #pragma once
 
 #include "attn.cuh"
@@ -46,14 +57,16 @@ struct Attn2Cfg {
   static constexpr int K_BYTES = BN * DHP * 2;
   static constexpr int V_BYTES = DHP * BN * 2;         // v^T tile: DHP rows x 128 keys
   static constexpr int KVST = 3;
-  static constexpr int SMEM = 2 * Q_BYTES + KVST * (K_BYTES + V_BYTES) + 256 + 1024;
+  static constexpr int XCH_FLOATS = 8 * 2 * 2 * 32 + 8 * 2 * 32;   // half-row maxima [pair][half][slot][row], sums
+  static constexpr int SMEM = 2 * Q_BYTES + KVST * (K_BYTES + V_BYTES) + 256 + XCH_FLOATS * 4 + 1024;
+  static constexpr int THREADS = 640;
   static constexpr int S_COL = 0;      // + 128 * t
   static constexpr int P_COL = 256;    // + 64 * t
   static constexpr int O_COL = 384;    // + 64 * t
 };
 
 template <int DHP, bool KMASK>   // KMASK: a key-padding mask may be given
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(640, 1)
     attn2_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                  const __grid_constant__ CUtensorMap map_vt, AttnArgs args, DevStatus* status) {
   using C = Attn2Cfg<DHP>;
@@ -75,6 +88,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* mma_done = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 18);   // bars 18-19
+  float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = args.S;
@@ -91,8 +105,8 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], 4);
-      mbar_init(&p_full[t], 4);
+      mbar_init(&s_free[t], 8);
+      mbar_init(&p_full[t], 8);
       mbar_init(&pv_done[t], 1);
     }
     mbar_init(mma_done, 3);
@@ -234,16 +248,31 @@ __global__ void __launch_bounds__(384, 1)
       umma_commit(mma_done);
       mbar_drain(mma_done, 0);
     }
-  } else if (warp >= 4) {  // ================= softmax: tile t, one query row per thread
-    const int t = (warp - 4) >> 2;
+  } else {  // ================= softmax: tile t, key half c, one query row per thread
+    // Two warps on the same scheduler share each 32-row quarter of a tile:
+    // warp (t, c=0) takes keys [0, 64) of every 128-key tile, (t, c=1) keys
+    // [64, 128). They agree on the row maximum through shared memory and a
+    // 64-thread named barrier once per key tile, and on the row sum at the end.
+    const int sw = warp - 4;
+    const int t = sw >> 3;
+    const int c = (sw >> 2) & 1;
     const int qd = warp & 3;
     const int row = qd * 32 + lane;
+    const int pair = t * 4 + qd;
+    const uint32_t bar_id = 1 + pair;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    const uint32_t t_s = tmem_base + lane_off + C::S_COL + t * 128;
-    const uint32_t t_p = tmem_base + lane_off + C::P_COL + t * 64;
-    const uint32_t t_o = tmem_base + lane_off + C::O_COL + t * 64;
+    const uint32_t t_s = tmem_base + lane_off + C::S_COL + t * 128 + 64 * c;
+    const uint32_t t_p = tmem_base + lane_off + C::P_COL + t * 64 + 32 * c;
+    constexpr int OH = DHP >= 64 ? DHP / 2 : DHP;   // O columns this warp rescales and stores
+    const bool o_mine = DHP >= 64 || c == 0;
+    const int ocol0 = DHP >= 64 ? OH * c : 0;
+    const uint32_t t_o = tmem_base + lane_off + C::O_COL + t * 64 + ocol0;
+    float* xm_own = xch + ((pair * 2 + c) * 2) * 32;
+    const float* xm_oth = xch + ((pair * 2 + (1 - c)) * 2) * 32;
+    float* xl_own = xch + 8 * 2 * 2 * 32 + (pair * 2 + c) * 32;
+    const float* xl_oth = xch + 8 * 2 * 2 * 32 + (pair * 2 + (1 - c)) * 32;
     const float sl2 = args.scale_log2;
-    int ns = 0, np = 0;   // S tiles read and P tiles written by this tile's softmax so far
+    int ns = 0, np = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
       const int nqt = item_nqt(item);
@@ -255,49 +284,46 @@ __global__ void __launch_bounds__(384, 1)
       float m_use = 0.f, l = 0.f;
       const uint8_t* mrow = (KMASK && args.kmask) ? args.kmask + (long long)(bh / args.H) * S : nullptr;
       for (int j = 0; j < nkv; ++j) {
-        uint32_t kb[BN / 32];
-        if (KMASK && mrow) key_mask_load<BN / 32>(mrow, j * BN, S, lane, kb);
+        const int kv0 = j * BN + 64 * c;   // first key of this half
+        uint32_t kb[2];
+        if (KMASK && mrow) key_mask_load<2>(mrow, kv0, S, lane, kb);
         if (!mbar_wait_warp(&s_full[t], ns & 1, wc)) { ok = false; break; }
         tc_fence_after();
-        float s[BN];
+        float s[64];
         {
-          uint32_t r[BN];   // the whole score row in one TMEM load
-          tmem_ld128(t_s, r);
+          uint32_t r[64];
+          tmem_ld64(t_s, r);
 #pragma unroll
-          for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(r[i]);
+          for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
         }
-        // S_t is in registers: the issuer may compute the next S into it.
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[t]);
         ++ns;
-
-        const int kv0 = j * BN;
-        const bool need_mask = (kv0 + BN > S) || (args.causal && kv0 + BN - 1 > q0);
+        const bool need_mask = (kv0 + 64 > S) || (args.causal && kv0 + 63 > q0);
         if (need_mask) {
-          const int lim = args.causal ? min(S, qpos + 1) : S;  // keys [0, lim) are visible
+          const int lim = args.causal ? min(S, qpos + 1) : S;
 #pragma unroll
-          for (int c = 0; c < BN; ++c)
-            if (kv0 + c >= lim) s[c] = -INFINITY;
+          for (int i = 0; i < 64; ++i)
+            if (kv0 + i >= lim) s[i] = -INFINITY;
         }
-        if (KMASK && mrow) {   // key padding: invalid keys get probability 0 (-inf score)
-          key_mask_ballot<BN / 32>(kb);
-          uint32_t all = kb[0];
+        if (KMASK && mrow) {
+          key_mask_ballot<2>(kb);
+          if ((kb[0] & kb[1]) != 0xffffffffu) {
 #pragma unroll
-          for (int w = 1; w < BN / 32; ++w) all &= kb[w];
-          if (all != 0xffffffffu) {
-#pragma unroll
-            for (int c = 0; c < BN; ++c)
-              if (!((kb[c >> 5] >> (c & 31)) & 1u)) s[c] = -INFINITY;
+            for (int i = 0; i < 64; ++i)
+              if (!((kb[i >> 5] >> (i & 31)) & 1u)) s[i] = -INFINITY;
           }
         }
-        // Row max: eight independent chains of three-input maxima.
         float m8[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) m8[k] = fmaxf(s[2 * k], s[2 * k + 1]);
 #pragma unroll
-        for (int i = 8; i < BN / 2; ++i) m8[i & 7] = fmax3f(m8[i & 7], s[2 * i], s[2 * i + 1]);
-        const float mx = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+        for (int i = 8; i < 32; ++i) m8[i & 7] = fmax3f(m8[i & 7], s[2 * i], s[2 * i + 1]);
+        const float hm = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+        xm_own[(j & 1) * 32 + lane] = hm;
+        asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+        const float mx = fmaxf(hm, xm_oth[(j & 1) * 32 + lane]);
         const float m_cand = mx * sl2;
         float alpha = 1.f;
         bool rescale = false;
@@ -308,15 +334,12 @@ __global__ void __launch_bounds__(384, 1)
           m_use = m_cand;
           rescale = true;
         }
-        // p = 2^(s*scale*log2e - m) as fp16 pairs, held in registers until the
-        // P buffer is free. Pairs go through packed fp32x2 FMA/add,
-        // exponentials through MUFU.
         const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_use, -m_use);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
-        uint32_t pk[BN / 2];
+        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < BN / 2; ++i) {
+        for (int i = 0; i < 32; ++i) {
           const float2 xx = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), sc2, nm2);
           const float2 pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
           acc[i & 3] = __fadd2_rn(acc[i & 3], pp);
@@ -324,49 +347,54 @@ __global__ void __launch_bounds__(384, 1)
         }
         const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
         l = l * alpha + ((a01.x + a01.y) + (a23.x + a23.y));
-        // The previous P v must have read P_t and finished accumulating O_t.
         if (np > 0) {
           if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
           tc_fence_after();
         }
-        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-          for (int c = 0; c < DHP / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(t_o + c * 32, r);
+        if (j > 0 && o_mine && __any_sync(0xffffffffu, rescale)) {
+          uint32_t r[OH];
+          if constexpr (OH == 32) tmem_ld32(t_o, *reinterpret_cast<uint32_t(*)[32]>(r));
+          else tmem_ld64(t_o, *reinterpret_cast<uint32_t(*)[64]>(r));
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(t_o + c * 32, r);
-          }
+          for (int i = 0; i < OH; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          if constexpr (OH == 32) tmem_st32(t_o, *reinterpret_cast<uint32_t(*)[32]>(r));
+          else tmem_st64(t_o, *reinterpret_cast<uint32_t(*)[64]>(r));
         }
-        tmem_st64(t_p, pk);
+        tmem_st32(t_p, pk);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
         ++np;
       }
       if (!ok) break;
-      // ---- epilogue: ctx row = O / l (fp16); rows beyond S are not stored.
+      // ---- epilogue: the two halves' row sums, then ctx = O / l (fp16).
+      xl_own[lane] = l;
+      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+      const float lt = l + xl_oth[lane];
       if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
       tc_fence_after();
-      const float inv_l = l > 0.f ? 1.0f / l : 0.f;   // a row with every key masked -> 0
-      const int b = bh / args.H, h = bh % args.H;
-      __half* dst = args.ctx + ((long long)b * S + qpos) * args.d + (long long)h * args.dh;
+      if (o_mine) {
+        const float inv_l = lt > 0.f ? 1.0f / lt : 0.f;
+        const int b = bh / args.H, h = bh % args.H;
+        __half* dst = args.ctx + ((long long)b * S + qpos) * args.d + (long long)h * args.dh + ocol0;
 #pragma unroll 1
-      for (int c = 0; c < DHP / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_o + c * 32, r);
-        if (qpos < S && c * 32 < args.dh) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+        for (int cc = 0; cc < OH / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(t_o + cc * 32, r);
+          if (qpos < S && ocol0 + cc * 32 < args.dh) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            d4[v] = make_uint4(pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l),
-                               pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l),
-                               pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l),
-                               pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l));
+            for (int v = 0; v < 4; ++v) {
+              d4[v] = make_uint4(pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l),
+                                 pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l),
+                                 pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l),
+                                 pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l));
+            }
           }
         }
       }
+      // The next item's first exchange reuses xl / xm slots only after both
+      // warps have passed its named barrier, which they reach after this read.
       tc_fence_before();
     }
   }

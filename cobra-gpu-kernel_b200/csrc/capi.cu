@@ -344,7 +344,7 @@ int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& de
     if (rc) return rc;
     const long long items = (long long)BH * ((p.S + 255) / 256);
     const int grid = items < dev.sms ? (int)items : dev.sms;
-    kern<<<grid, 384, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
+    kern<<<grid, Attn2Cfg<DHP>::THREADS, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
     return check_launch("attn2_kernel");
   } else {
     auto kern = a.kmask ? attn_kernel<DHP, BN, true> : attn_kernel<DHP, BN, false>;
@@ -681,6 +681,32 @@ int b200l_row_layernorm(const float* x, float* y, const float* w, const float* b
   int rc = device_info(&dev);
   if (rc) return rc;
   return launch_row_ln<false>(x, y, w, b, eps, rows, d, static_cast<cudaStream_t>(stream), row_mask);
+}
+
+int b200l_convert(const void* src, int32_t src_type, void* dst, int32_t dst_type, int64_t n, void* stream) {
+  if (!src || !dst) return fail(B200L_ERR_NULL_POINTER, "convert: NULL pointer");
+  if (n <= 0) return fail(B200L_ERR_BAD_SHAPE, "convert: n must be positive");
+  if (src_type < 0 || src_type > 2 || dst_type < 0 || dst_type > 2)
+    return fail(B200L_ERR_BAD_SHAPE, "convert: element types must be B200L_DTYPE_F32 / _F16 / _BF16");
+  if (reinterpret_cast<uintptr_t>(src) % 16 || reinterpret_cast<uintptr_t>(dst) % 16)
+    return fail(B200L_ERR_ALIGNMENT, "convert: src and dst must be 16-byte aligned");
+  if (src_type == dst_type) return fail(B200L_ERR_BAD_SHAPE, "convert: source and destination types are the same");
+  DevInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  const long long vecs = (n + 7) / 8;
+  const int blocks = (int)((vecs + 255) / 256 < 8L * dev.sms ? (vecs + 255) / 256 : 8L * dev.sms);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto go = [&](auto kern) {
+    kern<<<blocks, 256, 0, st>>>(src, dst, (long long)n);
+    return check_launch("convert_kernel");
+  };
+  if (src_type == kF32 && dst_type == kF16) return go(convert_kernel<kF32, kF16>);
+  if (src_type == kF32) return go(convert_kernel<kF32, kBF16>);
+  if (src_type == kF16 && dst_type == kF32) return go(convert_kernel<kF16, kF32>);
+  if (src_type == kF16) return go(convert_kernel<kF16, kBF16>);
+  if (dst_type == kF32) return go(convert_kernel<kBF16, kF32>);
+  return go(convert_kernel<kBF16, kF16>);
 }
 
 int b200l_cast_f16(const float* src, void* dst, int64_t n, void* stream) {

@@ -11,6 +11,8 @@
 // rows of the output (:170-172).
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace b200l {
@@ -105,6 +107,70 @@ __global__ void pack_weights_kernel(int d, const float* __restrict__ wq, const f
 __global__ void cast_f16_kernel(const float* __restrict__ src, __half* __restrict__ dst, long long n) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     dst[i] = __float2half_rn(src[i]);
+}
+
+// dst = src converted between fp32 / fp16 / bf16 (round to nearest even),
+// eight elements per thread and step (16-byte fp16 / bf16 accesses): the
+// boundary conversion for reduced-precision inputs and outputs.
+enum ElemType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+
+template <int SRC, int DST>
+__global__ void convert_kernel(const void* __restrict__ src, void* __restrict__ dst, long long n) {
+  const long long n8 = n / 8;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8 + (n % 8 ? 1 : 0); i += stride) {
+    float v[8];
+    const long long e0 = i * 8;
+    const int cnt = (e0 + 8 <= n) ? 8 : (int)(n - e0);
+    if (cnt == 8) {
+      if constexpr (SRC == kF32) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src) + 2 * i);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 2 * i + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(src) + i);
+        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float2 f;
+          if constexpr (SRC == kF16) f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+          else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+          v[2 * k] = f.x; v[2 * k + 1] = f.y;
+        }
+      }
+    } else {
+      for (int k = 0; k < cnt; ++k) {
+        if constexpr (SRC == kF32) v[k] = reinterpret_cast<const float*>(src)[e0 + k];
+        else if constexpr (SRC == kF16) v[k] = __half2float(reinterpret_cast<const __half*>(src)[e0 + k]);
+        else v[k] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[e0 + k]);
+      }
+    }
+    if (cnt == 8) {
+      if constexpr (DST == kF32) {
+        reinterpret_cast<float4*>(dst)[2 * i] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(dst)[2 * i + 1] = make_float4(v[4], v[5], v[6], v[7]);
+      } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if constexpr (DST == kF16) {
+            const __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+            w[k] = *reinterpret_cast<const uint32_t*>(&h);
+          } else {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+            w[k] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+        }
+        reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+      for (int k = 0; k < cnt; ++k) {
+        if constexpr (DST == kF32) reinterpret_cast<float*>(dst)[e0 + k] = v[k];
+        else if constexpr (DST == kF16) reinterpret_cast<__half*>(dst)[e0 + k] = __float2half_rn(v[k]);
+        else reinterpret_cast<__nv_bfloat16*>(dst)[e0 + k] = __float2bfloat16_rn(v[k]);
+      }
+    }
+  }
 }
 
 // Test hook: arms a fault-injection site and a per-wait time limit in a

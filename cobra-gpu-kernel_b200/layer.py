@@ -34,6 +34,7 @@ import torch.nn as nn
 from . import _lib
 
 GRAPH_MAX_INPUT_BYTES = 64 * 1024 * 1024   # reference gate, torch_transformer_benchmark.py:1077-1079
+_REDUCED = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16}   # converted at the boundary
 HOST_CHUNK_BYTES = 16 * 1024 * 1024        # about this many x bytes per chunk when streaming a host batch
 
 
@@ -343,8 +344,10 @@ class B200TransformerLayer(nn.Module):
         (no CUDA-graph replay, no static buffer); it is returned."""
         if x.dim() != 3 or x.shape[-1] != self.attention.d_model:
             raise ValueError(f"expected x of shape [B, S, {self.attention.d_model}], got {tuple(x.shape)}")
+        if x.dtype in _REDUCED:
+            return self._forward_reduced(x, valid_token_mask, out)
         if x.dtype != torch.float32:
-            raise TypeError(f"B200TransformerLayer computes fp32-in/fp32-out; got {x.dtype}")
+            raise TypeError(f"B200TransformerLayer takes fp32, fp16 or bf16 x; got {x.dtype}")
         if out is not None and (not x.is_cuda or out.device != x.device or out.shape != x.shape
                                 or out.dtype != torch.float32 or not out.is_contiguous()):
             raise ValueError("out must be a contiguous fp32 tensor of x's shape on x's (CUDA) device")
@@ -380,6 +383,33 @@ class B200TransformerLayer(nn.Module):
             y = out if out is not None else torch.empty_like(x)
             self._launch(x, y, desc)
             return y
+
+    def _forward_reduced(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
+                         out: Optional[torch.Tensor]) -> torch.Tensor:
+        """fp16 / bf16 x (the reference's --dtype float16 / bfloat16 modes,
+        torch_transformer_benchmark.py:952-962): converted to fp32 on the GPU
+        by b200l_convert, run through the fp32 layer, and y converted back to
+        x's dtype (round to nearest even). A host-resident x is widened on the
+        host and streamed as fp32."""
+        code = _REDUCED[x.dtype]
+        if not x.is_cuda:
+            if out is not None:
+                raise ValueError("out= needs a CUDA x")
+            return self.forward(x.float(), valid_token_mask).to(x.dtype)
+        if out is not None and (out.device != x.device or out.shape != x.shape or out.dtype != x.dtype
+                                or not out.is_contiguous()):
+            raise ValueError("out must be a contiguous tensor of x's shape, dtype and device")
+        x = x.contiguous()
+        L = _lib.lib()
+        n = x.numel()
+        with torch.cuda.device(x.device):
+            st = torch.cuda.current_stream(x.device).cuda_stream
+            x32 = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+            _lib.check(L.b200l_convert(x.data_ptr(), code, x32.data_ptr(), _lib.DTYPE_F32, n, st))
+            y32 = self.forward(x32, valid_token_mask)
+            y = out if out is not None else torch.empty(x.shape, dtype=x.dtype, device=x.device)
+            _lib.check(L.b200l_convert(y32.data_ptr(), _lib.DTYPE_F32, y.data_ptr(), code, n, st))
+        return y
 
     def warmup(self, seq_len: int, device: torch.device, with_mask: bool = False) -> None:
         """Pack the weights and run one single-sequence forward of this shape

@@ -225,6 +225,17 @@ B200L_API int b200l_row_layernorm(const float* x, float* y, const float* w, cons
  * 873-914) for ffn_in / ffn_out. */
 B200L_API int b200l_cast_f16(const float* src, void* dst, int64_t n, void* stream);
 
+/* dst = src converted between element types (round to nearest even), n
+ * elements, both 16-byte aligned: the boundary conversion that lets the fp32
+ * layer take and return fp16 / bf16 tensors (the reference's
+ * --dtype float16 / bfloat16 harness modes, torch_transformer_benchmark.py:
+ * 952-962, :1091-1094, run the same layer in that dtype). */
+#define B200L_DTYPE_F32 0
+#define B200L_DTYPE_F16 1
+#define B200L_DTYPE_BF16 2
+B200L_API int b200l_convert(const void* src, int32_t src_type, void* dst, int32_t dst_type, int64_t n,
+                            void* stream);
+
 /* Allocation-free variant of b200l_layer_forward. No counterpart in the
  * reference (its Python module always allocates through PyTorch).
  *

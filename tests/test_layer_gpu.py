@@ -242,7 +242,7 @@ def test_error_codes(pkg, cuda_ok):
     with pytest.raises(ValueError):
         lay(torch.zeros(2, 3, 64, device="cuda"))
     with pytest.raises(TypeError):
-        lay(torch.zeros(2, 3, 128, device="cuda", dtype=torch.float16))
+        lay(torch.zeros(2, 3, 128, device="cuda", dtype=torch.float64))
     bad = pkg.B200TransformerLayer(48, 3).cuda()      # head_dim 16: unsupported
     with pytest.raises(pkg._lib.B200LError, match="head_dim 16 unsupported"):
         bad(torch.zeros(1, 4, 48, device="cuda"))
