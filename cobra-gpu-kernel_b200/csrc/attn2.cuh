@@ -26,8 +26,11 @@
 //   * warps 4-19 are the softmax: warp 4 + 8t + 4c + q handles rows
 //     32q..32q+31 of tile t and keys [64c, 64c + 64) of every 128-key tile;
 //     the two warps of a row agree on the row maximum through shared memory
-//     and a 64-thread named barrier once per key tile, and add their row sums
-//     at the end of the item;
+//     and a 64-thread named barrier once per key tile (every path of both
+//     warps reaches it once per step, a warp that gave up after a timed-out
+//     wait signalling so in the exchanged value, so a warp never waits there
+//     for a partner that is gone), and add their row sums at the end of the
+//     item;
 //   * per tile, TMEM holds S (fp32, 128 columns), P (fp16 pairs, 64 columns)
 //     and O (fp32, dhp columns): the softmax releases S as soon as its half
 //     row is in registers, so the next S = Q K^T is computed while the
@@ -47,6 +50,11 @@
 #include "common.cuh"
 
 namespace b200l {
+
+// Value a softmax warp writes in place of its row data when it leaves the
+// item loop after a timed-out wait (a quiet NaN with a payload that neither
+// the max of scores nor a row sum produces).
+constexpr uint32_t kPairLeft = 0x7FDEAD01u;
 
 template <int DHP>
 struct Attn2Cfg {
@@ -251,15 +259,15 @@ __global__ void __launch_bounds__(640, 1)
   } else {  // ================= softmax: tile t, key half c, one query row per thread
     // Two warps on the same scheduler share each 32-row quarter of a tile:
     // warp (t, c=0) takes keys [0, 64) of every 128-key tile, (t, c=1) keys
-    // [64, 128). They agree on the row maximum through shared memory and a
-    // 64-thread named barrier once per key tile, and on the row sum at the end.
+    // [64, 128). They agree on the row maximum through shared memory and the
+    // pair's named barrier once per key tile, and on the row sum at the end
+    // of the item.
     const int sw = warp - 4;
     const int t = sw >> 3;
     const int c = (sw >> 2) & 1;
     const int qd = warp & 3;
     const int row = qd * 32 + lane;
     const int pair = t * 4 + qd;
-    const uint32_t bar_id = 1 + pair;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
     const uint32_t t_s = tmem_base + lane_off + C::S_COL + t * 128 + 64 * c;
     const uint32_t t_p = tmem_base + lane_off + C::P_COL + t * 64 + 32 * c;
@@ -272,6 +280,14 @@ __global__ void __launch_bounds__(640, 1)
     float* xl_own = xch + 8 * 2 * 2 * 32 + (pair * 2 + c) * 32;
     const float* xl_oth = xch + 8 * 2 * 2 * 32 + (pair * 2 + (1 - c)) * 32;
     const float sl2 = args.scale_log2;
+    const uint32_t bar_id = 1 + pair;   // named barrier of the two warps of this row pair
+    // Both warps of a pair meet at the pair barrier exactly once per key tile
+    // and once at the end of an item, on every path. A warp whose bounded wait
+    // ran out still meets its partner there, having written kPairLeft (a NaN
+    // bit pattern no arithmetic here produces) instead of its value, and both
+    // warps leave together: a warp never waits at the barrier for a partner
+    // that is gone, and every wait before it is bounded.
+    const uint32_t left_bits = kPairLeft;
     int ns = 0, np = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
@@ -287,7 +303,13 @@ __global__ void __launch_bounds__(640, 1)
         const int kv0 = j * BN + 64 * c;   // first key of this half
         uint32_t kb[2];
         if (KMASK && mrow) key_mask_load<2>(mrow, kv0, S, lane, kb);
-        if (!mbar_wait_warp(&s_full[t], ns & 1, wc)) { ok = false; break; }
+        if (!mbar_wait_warp(&s_full[t], ns & 1, wc)) {
+          xm_own[(j & 1) * 32 + lane] = __uint_as_float(left_bits);
+          xl_own[lane] = __uint_as_float(left_bits);
+          asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+          ok = false;
+          break;
+        }
         tc_fence_after();
         float s[64];
         {
@@ -321,9 +343,13 @@ __global__ void __launch_bounds__(640, 1)
 #pragma unroll
         for (int i = 8; i < 32; ++i) m8[i & 7] = fmax3f(m8[i & 7], s[2 * i], s[2 * i + 1]);
         const float hm = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+        // Exchange the half-row maxima (two slots by step parity: a warp is
+        // never more than one step ahead of its partner).
         xm_own[(j & 1) * 32 + lane] = hm;
         asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-        const float mx = fmaxf(hm, xm_oth[(j & 1) * 32 + lane]);
+        const float hp = xm_oth[(j & 1) * 32 + lane];
+        if (__any_sync(0xffffffffu, __float_as_uint(hp) == left_bits)) { ok = false; break; }
+        const float mx = fmaxf(hm, hp);
         const float m_cand = mx * sl2;
         float alpha = 1.f;
         bool rescale = false;
@@ -348,7 +374,13 @@ __global__ void __launch_bounds__(640, 1)
         const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
         l = l * alpha + ((a01.x + a01.y) + (a23.x + a23.y));
         if (np > 0) {
-          if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
+          if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) {   // meets the partner's next exchange
+            xm_own[((j + 1) & 1) * 32 + lane] = __uint_as_float(left_bits);
+            xl_own[lane] = __uint_as_float(left_bits);
+            asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+            ok = false;
+            break;
+          }
           tc_fence_after();
         }
         if (j > 0 && o_mine && __any_sync(0xffffffffu, rescale)) {
@@ -367,11 +399,14 @@ __global__ void __launch_bounds__(640, 1)
         ++np;
       }
       if (!ok) break;
-      // ---- epilogue: the two halves' row sums, then ctx = O / l (fp16).
-      xl_own[lane] = l;
+      // ---- epilogue: the two halves' row sums, then ctx = O / l (fp16). The
+      // pair barrier again carries a failure of either warp.
+      const bool fine_e = mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc);
+      xl_own[lane] = fine_e ? l : __uint_as_float(left_bits);
       asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-      const float lt = l + xl_oth[lane];
-      if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
+      const float lp = xl_oth[lane];
+      if (!fine_e || __any_sync(0xffffffffu, __float_as_uint(lp) == left_bits)) { ok = false; break; }
+      const float lt = l + lp;
       tc_fence_after();
       if (o_mine) {
         const float inv_l = lt > 0.f ? 1.0f / lt : 0.f;

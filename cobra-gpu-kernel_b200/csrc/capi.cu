@@ -278,6 +278,51 @@ int launch_gemm_tma_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
   return check_launch("gemm_tma_kernel");
 }
 
+// Clusters of NC CTAs for the LayerNorm-2 out-projection (d = 256 NC): the
+// persistent grid holds as many clusters as can be resident at once (looked
+// up once per device and kernel), at most one per M tile.
+template <int NC, int ST>
+int launch_gemm_ln_cluster_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const EpiArgs& ea, long long T,
+                             int K, void* ws, cudaStream_t st) {
+  auto kern = gemm_ln_cluster_kernel<NC, ST>;
+  const int smem = GemmLnClusterCfg<ST>::SMEM;
+  int rc = ensure_smem((const void*)kern, smem);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = NC;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B200L_ERR_DEVICE, "device ordinal %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (max_clusters[dev] == 0) {
+      cfg.gridDim = dim3(NC * 16, 1, 1);
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, (const void*)kern, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+      if (n <= 0) return fail(B200L_ERR_LAUNCH, "no cluster of %d CTAs fits on this device", NC);
+      max_clusters[dev] = n;
+    }
+  }
+  const long long MT = (T + 127) / 128;
+  const long long ncl = MT < max_clusters[dev] ? MT : max_clusters[dev];
+  cfg.gridDim = dim3((unsigned)(ncl * NC), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, map_a, map_b, ea, T, K, reinterpret_cast<DevStatus*>(ws));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemm_ln_cluster_kernel)");
+  return check_launch("gemm_ln_cluster_kernel");
+}
+
 int run_qkv(const b200l_layer_desc* desc, const Plan& p, const float* x, void* ws, cudaStream_t st) {
   if (p.d <= 256) {
     const int kp = (p.d + 63) / 64 * 64;
@@ -392,6 +437,17 @@ int run_outproj(const b200l_layer_desc* desc, const Plan& p, const float* x, flo
     }
   }
   if ((rc = map_rows_k(&map_b, desc->wo, (unsigned long long)p.d, p.d, 256, "wo"))) return rc;
+  // d = 256 NC: a cluster of NC CTAs shares each row tile and completes LN2 in
+  // the epilogue (row statistics exchanged through distributed shared memory).
+  switch (p.d) {
+    case 512: return launch_gemm_ln_cluster_t<2, 4>(map_a, map_b, ea, p.T, p.d, ws, st);
+    case 768: return launch_gemm_ln_cluster_t<3, 4>(map_a, map_b, ea, p.T, p.d, ws, st);
+    case 1024: return launch_gemm_ln_cluster_t<4, 4>(map_a, map_b, ea, p.T, p.d, ws, st);
+    case 1536: return launch_gemm_ln_cluster_t<6, 4>(map_a, map_b, ea, p.T, p.d, ws, st);
+    case 2048: return launch_gemm_ln_cluster_t<8, 3>(map_a, map_b, ea, p.T, p.d, ws, st);
+    default: break;
+  }
+  // Other widths: the residual in the GEMM epilogue, then a row LayerNorm pass.
   if ((rc = launch_gemm_tma_t<256, 4, EPI_RESID>(map_a, map_b, ea, p.T, p.d, p.d, ws, st))) return rc;
   return launch_row_ln<false>(y, y, desc->ln2_w, desc->ln2_b, desc->eps2, p.T, p.d, st, nullptr);
 }

@@ -154,6 +154,84 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, W
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, wc));
 }
 
+// ---------------------------------------------------------------------------
+// Thread-block clusters: distributed shared memory and cross-CTA barriers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t caddr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(caddr), "f"(a), "f"(b) : "memory");
+}
+// Arrive on an mbarrier in (possibly) another CTA of the cluster, releasing
+// this thread's earlier shared-memory writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire: after it, shared-memory writes that
+// other CTAs released by arriving on this barrier are visible.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, WaitCtl* wc) {
+  const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long lim = wc->limit_ns;
+#pragma unroll 1
+  while (!mbar_try_wait_acq_cluster(bar, parity)) {
+    if (waitctl_aborted(wc)) return false;
+    if (globaltimer_ns() - t0 > lim) {
+      *reinterpret_cast<volatile int*>(&wc->abort) = 1;
+      return false;
+    }
+  }
+  return true;
+}
+// Named barrier `id` over `count` threads (whole warps) that also returns the
+// OR of every participant's `pred`: warps use it to leave a loop together.
+__device__ __forceinline__ bool pair_barrier_any(bool pred, uint32_t id, uint32_t count = 64) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+// Every thread of every CTA of the cluster arrives, then waits (whole warps).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
 // Wait used only while unwinding: ignores the abort flag, bounded by time.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();

@@ -608,4 +608,255 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ===========================================================================
+// Out-projection with the residual and LayerNorm-2 in the epilogue for
+// d_model = NC * 256 > 256: y = LN2(x + ctx Wo^T + bo).
+//
+// A 256-column accumulator per CTA cannot see a whole row, so a cluster of NC
+// CTAs shares each 128-row M tile, CTA rank r owning output columns
+// [256 r, 256 r + 256). Each epilogue thread (one row) forms r = x + acc + bo
+// for its 256 columns (written back to TMEM), its mean and the sum of squared
+// deviations about it (two passes over TMEM), stores that pair into every CTA
+// of the cluster (distributed shared memory) and arrives on each CTA's stats
+// barrier with cluster-scope release. After the
+// cluster-scope acquire, each thread combines the NC pairs (equal counts:
+// mean = average of the means, M2 = sum of M2 + 256 * sum of squared mean
+// offsets), normalises its 256 columns from TMEM and stores y. The residual
+// is added in fp32 before any rounding, as in EPI_RESID_LN (reference
+// _gemm_ln_kernel, torch_transformer_benchmark.py:394-463, which needs the
+// whole row in one tile; the reference's fallback for wider rows is a
+// separate _add_ln_kernel pass, :1289-1292 -- this kernel removes that pass).
+// Every CTA of a cluster walks the same M tiles (cluster c: tiles c, c +
+// nclusters, ...), with the TMA producer and the MMA issuer running ahead
+// into the second TMEM accumulator. No TMA load uses cluster multicast: each
+// CTA loads its own A tile and its 256 rows of Wo.
+// ===========================================================================
+template <int ST>
+struct GemmLnClusterCfg {
+  static constexpr int BN = 256;
+  static constexpr int A_BYTES = 128 * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STATS_BYTES = 2 * 8 * 128 * 8;   // [slot][rank <= 8][row] (mean, M2)
+  static constexpr int SMEM = ST * STAGE + 256 + STATS_BYTES + 1024;
+};
+
+template <int NC, int ST>
+__global__ void __launch_bounds__(192, 1)
+    gemm_ln_cluster_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                           EpiArgs ea, long long T, int K, DevStatus* status) {
+  using C = GemmLnClusterCfg<ST>;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST * C::STAGE);
+  uint64_t* full = bars;                    // [ST]
+  uint64_t* empty = bars + ST;              // [ST]
+  uint64_t* acc_full = bars + 2 * ST;       // [2]
+  uint64_t* acc_empty = bars + 2 * ST + 2;  // [2], one arrival per epilogue warp
+  uint64_t* stats_full = bars + 2 * ST + 4; // [2], one arrival per epilogue thread of each CTA of the cluster
+  uint64_t* mma_done = bars + 2 * ST + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 7);
+  WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 2 * ST + 8);   // 2 slots
+  float2* stats = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + 256);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const long long MT = (T + 127) / 128;
+  const long long cid = cluster_id_x(), ncl = cluster_count_x();
+  const int n0 = (int)rank * BN;
+  const int KT = (K + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+      mbar_init(&stats_full[a], NC * 128);
+    }
+    mbar_init(mma_done, 1);
+    waitctl_init(wc, status);
+    fence_barrier_init();
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  // Every CTA's barriers are initialised before any peer may arrive on them.
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- producer: A / B k-tiles of every M tile of this cluster
+      int last[ST];
+      for (int i = 0; i < ST; ++i) last[i] = -1;
+      long long it = 0;
+      bool ok = true;
+      for (long long mt = cid; mt < MT && ok; mt += ncl) {
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = (int)(it % ST);
+          if (!mbar_wait(&empty[s], (uint32_t)((it / ST) & 1) ^ 1u, wc)) { ok = false; break; }
+          if (it == 0 && cid == 0 && rank == 0 && wc->site == kSiteGemmOperand) continue;   // test hook
+          mbar_arrive_expect_tx(&full[s], C::STAGE);
+          uint8_t* st = smem + s * C::STAGE;
+          tma_load_2d(st, &map_a, &full[s], kt * 64, (int)(mt * 128));
+          tma_load_2d(st + C::A_BYTES, &map_b, &full[s], kt * 64, n0);
+          last[s] = (int)(it / ST);
+        }
+      }
+      for (int s = 0; s < ST; ++s)
+        if (last[s] >= 0) mbar_drain(&full[s], last[s] & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      const uint32_t idesc = idesc_f16_f32(128, BN);
+      long long it = 0;
+      int ti = 0;
+      bool ok = true;
+      for (long long mt = cid; mt < MT && ok; mt += ncl, ++ti) {
+        const int a = ti & 1;
+        if (ti >= 2 && !mbar_wait(&acc_empty[a], ((ti >> 1) - 1) & 1, wc)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + a * BN;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = (int)(it % ST);
+          if (!mbar_wait(&full[s], (uint32_t)((it / ST) & 1), wc)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + s * C::STAGE);
+          const uint32_t b_base = a_base + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_ss(d_tmem, sdesc_kmajor(a_base + kk * 32, 128), sdesc_kmajor(b_base + kk * 32, 128), idesc,
+                        (kt | kk) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[a]);
+      }
+      umma_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+  } else {  // ---- epilogue warps 2..5, one output row per thread
+    const int qd = warp & 3;
+    const int row = qd * 32 + lane;
+    const int d = ea.d;
+    const float inv_d = 1.0f / (float)d;
+    int ti = 0;
+    for (long long mt = cid; mt < MT; mt += ncl, ++ti) {
+      const int a = ti & 1;
+      const long long t = mt * 128 + row;
+      const bool valid = t < T;
+      // A padded query row's attention output (bias included) is zeroed:
+      // y = LN2(x) there (BaselineSelfAttention, :121-122).
+      const bool keep = ea.rowmask == nullptr || (valid && ea.rowmask[t] != 0);
+      const uint32_t tl = tmem_base + a * BN + ((uint32_t)(qd * 32) << 16);
+      const float* xr = ea.x + t * d + n0;
+      if (!mbar_wait_warp(&acc_full[a], (uint32_t)(ti >> 1) & 1, wc)) break;
+      tc_fence_after();
+      // pass 1: r = x + (acc + b) back into TMEM; row sum of these columns.
+      float sum = 0.f;
+      float4 xn[8];
+      load_x_chunk(xr, 0, valid, BN, xn);
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        float4 xc[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) xc[c] = xn[c];
+        if (cc + 1 < BN / 32) load_x_chunk(xr, cc * 32 + 32, valid, BN, xn);
+        uint32_t r[32];
+        tmem_ld32(tl + cc * 32, r);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.bias + n0 + cc * 32) + c);
+          const float a0 = xc[c].x + (keep ? __uint_as_float(r[4 * c + 0]) + bv.x : 0.f);
+          const float a1 = xc[c].y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
+          const float a2 = xc[c].z + (keep ? __uint_as_float(r[4 * c + 2]) + bv.z : 0.f);
+          const float a3 = xc[c].w + (keep ? __uint_as_float(r[4 * c + 3]) + bv.w : 0.f);
+          sum += (a0 + a1) + (a2 + a3);
+          r[4 * c + 0] = __float_as_uint(a0);
+          r[4 * c + 1] = __float_as_uint(a1);
+          r[4 * c + 2] = __float_as_uint(a2);
+          r[4 * c + 3] = __float_as_uint(a3);
+        }
+        tmem_st32(tl + cc * 32, r);
+      }
+      const float mean_l = sum * (1.0f / (float)BN);
+      // pass 2: squared deviations about this CTA's own mean.
+      float m2 = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tl + cc * 32, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float dv = __uint_as_float(r[i]) - mean_l;
+          m2 += dv * dv;
+        }
+      }
+      // Exchange (mean, M2) of this row with every CTA of the cluster: store
+      // the pair into each CTA's slot, then arrive (cluster-scope release of
+      // that store) on each CTA's stats barrier, which expects one arrival
+      // per epilogue thread of every CTA. Every wait stays bounded.
+      const int slot = ti & 1;
+      const uint32_t my_entry = smem_u32(&stats[(slot * 8 + (int)rank) * 128 + row]);
+      const uint32_t bar_local = smem_u32(&stats_full[slot]);
+#pragma unroll 1
+      for (int q = 0; q < NC; ++q) {
+        st_cluster_v2(mapa_shared(my_entry, (uint32_t)q), mean_l, m2);
+        mbar_arrive_cluster(mapa_shared(bar_local, (uint32_t)q));
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(&stats_full[slot], (uint32_t)(ti >> 1) & 1, wc))) break;
+      float mean = 0.f;
+#pragma unroll
+      for (int q = 0; q < NC; ++q) mean += stats[(slot * 8 + q) * 128 + row].x;
+      mean *= 1.0f / (float)NC;
+      float M2 = 0.f;
+#pragma unroll
+      for (int q = 0; q < NC; ++q) {
+        const float2 e = stats[(slot * 8 + q) * 128 + row];
+        const float dm = e.x - mean;
+        M2 += e.y + (float)BN * dm * dm;
+      }
+      const float rstd = rsqrtf(M2 * inv_d + ea.eps);
+      // pass 3: normalise this CTA's columns and store y.
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tl + cc * 32, r);
+        if (valid) {
+          float* yr = ea.y + t * d + n0 + cc * 32;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int col = n0 + cc * 32 + 4 * c;
+            const float4 wv = __ldg(reinterpret_cast<const float4*>(ea.ln_w + col));
+            const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.ln_b + col));
+            float4 o;
+            o.x = (__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bv.x;
+            o.y = (__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bv.y;
+            o.z = (__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bv.z;
+            o.w = (__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bv.w;
+            reinterpret_cast<float4*>(yr)[c] = o;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && waitctl_aborted(wc)) record_error(status, kErrTimeout, kGemmTma, 10 + NC);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+  // No CTA leaves while a peer may still write into its shared memory.
+  cluster_sync_all();
+}
+
 }  // namespace b200l
