@@ -12,49 +12,41 @@
 //     own rate -- so the MMAs are spread over three issuing threads;
 //   * the exponentials (FFMA2 -> 2x MUFU ex2 -> FADD2 + fp16 pack per pair of
 //     scores) reach 74 % of MUFU throughput with one warp per scheduler, 90 %
-//     with two and 96 % with three or four -- so each 32-row quarter of a
-//     query tile is split over two warps by key halves, four softmax warps
-//     per scheduler;
+//     with two and 96 % with three or four -- so sixteen softmax warps, four
+//     per scheduler, each handling 16 rows with two threads per row;
 //   * under MUFU load every shared-memory / barrier / TMEM round trip of a
 //     warp costs 150-250 cycles, so each warp's step is a short fixed chain
-//     of them around its exponentials.
+//     of them around its exponentials, and the two halves of a row live in
+//     one warp (16x32bx2 TMEM loads / stores: threads 0-15 take keys [0, 64),
+//     threads 16-31 keys [64, 128) of the same 16 rows) so that they agree on
+//     the row maximum with one shuffle instead of a shared-memory exchange.
 // Structure:
 //   * a work item is (b, h, 256 queries) = two 128-row query tiles that share
 //     every K / v^T tile (one TMA load feeds both tiles' MMAs);
 //   * warp 1 issues S = Q K^T for both tiles, warps 2 and 3 issue P v for
 //     tile 0 and 1;
-//   * warps 4-19 are the softmax: warp 4 + 8t + 4c + q handles rows
-//     32q..32q+31 of tile t and keys [64c, 64c + 64) of every 128-key tile;
-//     the two warps of a row agree on the row maximum through shared memory
-//     and a 64-thread named barrier once per key tile (every path of both
-//     warps reaches it once per step, a warp that gave up after a timed-out
-//     wait signalling so in the exchanged value, so a warp never waits there
-//     for a partner that is gone), and add their row sums at the end of the
-//     item;
+//   * warps 4-19 are the softmax: warp 4 + 8t + 4hh + q handles rows
+//     32q + 16hh .. 32q + 16hh + 15 of tile t, thread l and l + 16 the two key
+//     halves of one row;
 //   * per tile, TMEM holds S (fp32, 128 columns), P (fp16 pairs, 64 columns)
-//     and O (fp32, dhp columns): the softmax releases S as soon as its half
-//     row is in registers, so the next S = Q K^T is computed while the
+//     and O (fp32, dhp columns): the softmax releases S as soon as its rows
+//     are in registers, so the next S = Q K^T is computed while the
 //     exponentials run; P waits in registers until the previous P v has read
 //     the P buffer, and tcgen05.mma reads P from TMEM as its A operand (P
 //     never touches shared memory);
 //   * K / v^T stream through a 3-stage TMA ring; lazy rescaling of O (only when
-//     a row max grows by more than 2^8; each half rescales its half of O).
+//     a row max grows by more than 2^8; each thread rescales its half of O).
 // TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 // O0 [384, 384+dhp) O1 [448, 448+dhp).
-// S issuer, per key tile j and tile t: S_t(j) once both halves of softmax t
-// have read S_t(j-1) (and K tile j has landed). P v issuer t: P_t(j) v_j once
-// both halves have written P_t(j).
+// S issuer, per key tile j and tile t: S_t(j) once the eight softmax warps of
+// tile t have read S_t(j-1) (and K tile j has landed). P v issuer t: P_t(j)
+// v_j once they have written P_t(j).
 #pragma once
 
 #include "attn.cuh"
 #include "common.cuh"
 
 namespace b200l {
-
-// Value a softmax warp writes in place of its row data when it leaves the
-// item loop after a timed-out wait (a quiet NaN with a payload that neither
-// the max of scores nor a row sum produces).
-constexpr uint32_t kPairLeft = 0x7FDEAD01u;
 
 template <int DHP>
 struct Attn2Cfg {
@@ -65,8 +57,7 @@ struct Attn2Cfg {
   static constexpr int K_BYTES = BN * DHP * 2;
   static constexpr int V_BYTES = DHP * BN * 2;         // v^T tile: DHP rows x 128 keys
   static constexpr int KVST = 3;
-  static constexpr int XCH_FLOATS = 8 * 2 * 2 * 32 + 8 * 2 * 32;   // half-row maxima [pair][half][slot][row], sums
-  static constexpr int SMEM = 2 * Q_BYTES + KVST * (K_BYTES + V_BYTES) + 256 + XCH_FLOATS * 4 + 1024;
+  static constexpr int SMEM = 2 * Q_BYTES + KVST * (K_BYTES + V_BYTES) + 256 + 1024;
   static constexpr int THREADS = 640;
   static constexpr int S_COL = 0;      // + 128 * t
   static constexpr int P_COL = 256;    // + 64 * t
@@ -96,7 +87,6 @@ __global__ void __launch_bounds__(640, 1)
   uint64_t* mma_done = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 18);   // bars 18-19
-  float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = args.S;
@@ -256,38 +246,25 @@ __global__ void __launch_bounds__(640, 1)
       umma_commit(mma_done);
       mbar_drain(mma_done, 0);
     }
-  } else {  // ================= softmax: tile t, key half c, one query row per thread
-    // Two warps on the same scheduler share each 32-row quarter of a tile:
-    // warp (t, c=0) takes keys [0, 64) of every 128-key tile, (t, c=1) keys
-    // [64, 128). They agree on the row maximum through shared memory and the
-    // pair's named barrier once per key tile, and on the row sum at the end
-    // of the item.
+  } else {  // ================= softmax: tile t, 16 query rows per warp, two threads per row
+    // Warp 4 + 8t + 4hh + qd handles rows 32qd + 16hh .. + 15 of tile t: the
+    // 16x32bx2 TMEM forms give threads 0-15 keys [0, 64) and threads 16-31
+    // keys [64, 128) of the same 16 rows, so the two halves of a row are
+    // lanes l and l + 16 of one warp and agree on the row maximum (and, at
+    // the end, the row sum) with one shuffle.
     const int sw = warp - 4;
     const int t = sw >> 3;
-    const int c = (sw >> 2) & 1;
+    const int hh = (sw >> 2) & 1;
     const int qd = warp & 3;
-    const int row = qd * 32 + lane;
-    const int pair = t * 4 + qd;
-    const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    const uint32_t t_s = tmem_base + lane_off + C::S_COL + t * 128 + 64 * c;
-    const uint32_t t_p = tmem_base + lane_off + C::P_COL + t * 64 + 32 * c;
-    constexpr int OH = DHP >= 64 ? DHP / 2 : DHP;   // O columns this warp rescales and stores
-    const bool o_mine = DHP >= 64 || c == 0;
-    const int ocol0 = DHP >= 64 ? OH * c : 0;
-    const uint32_t t_o = tmem_base + lane_off + C::O_COL + t * 64 + ocol0;
-    float* xm_own = xch + ((pair * 2 + c) * 2) * 32;
-    const float* xm_oth = xch + ((pair * 2 + (1 - c)) * 2) * 32;
-    float* xl_own = xch + 8 * 2 * 2 * 32 + (pair * 2 + c) * 32;
-    const float* xl_oth = xch + 8 * 2 * 2 * 32 + (pair * 2 + (1 - c)) * 32;
+    const int c = lane >> 4;                       // key half of this thread
+    const int row = qd * 32 + hh * 16 + (lane & 15);
+    const uint32_t lane_off = (uint32_t)(qd * 32 + hh * 16) << 16;
+    const uint32_t t_s = tmem_base + lane_off + C::S_COL + t * 128;
+    const uint32_t t_p = tmem_base + lane_off + C::P_COL + t * 64;
+    constexpr int OH = DHP / 2;                    // O columns of this thread: [OH c, OH c + OH)
+    const uint32_t t_o = tmem_base + lane_off + C::O_COL + t * 64;
+    const int ocol0 = OH * c;
     const float sl2 = args.scale_log2;
-    const uint32_t bar_id = 1 + pair;   // named barrier of the two warps of this row pair
-    // Both warps of a pair meet at the pair barrier exactly once per key tile
-    // and once at the end of an item, on every path. A warp whose bounded wait
-    // ran out still meets its partner there, having written kPairLeft (a NaN
-    // bit pattern no arithmetic here produces) instead of its value, and both
-    // warps leave together: a warp never waits at the barrier for a partner
-    // that is gone, and every wait before it is bounded.
-    const uint32_t left_bits = kPairLeft;
     int ns = 0, np = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
@@ -297,24 +274,19 @@ __global__ void __launch_bounds__(640, 1)
       const int bh = item / QP;
       const int q0 = (item % QP) * 256 + t * 128;
       const int qpos = q0 + row;
+      const int lim = args.causal ? min(S, qpos + 1) : S;   // keys [0, lim) are visible
       float m_use = 0.f, l = 0.f;
       const uint8_t* mrow = (KMASK && args.kmask) ? args.kmask + (long long)(bh / args.H) * S : nullptr;
       for (int j = 0; j < nkv; ++j) {
-        const int kv0 = j * BN + 64 * c;   // first key of this half
-        uint32_t kb[2];
-        if (KMASK && mrow) key_mask_load<2>(mrow, kv0, S, lane, kb);
-        if (!mbar_wait_warp(&s_full[t], ns & 1, wc)) {
-          xm_own[(j & 1) * 32 + lane] = __uint_as_float(left_bits);
-          xl_own[lane] = __uint_as_float(left_bits);
-          asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-          ok = false;
-          break;
-        }
+        const int kv0 = j * BN + 64 * c;   // first key of this thread's half
+        uint32_t kb[4];
+        if (KMASK && mrow) key_mask_load<4>(mrow, j * BN, S, lane, kb);
+        if (!mbar_wait_warp(&s_full[t], ns & 1, wc)) { ok = false; break; }
         tc_fence_after();
         float s[64];
         {
           uint32_t r[64];
-          tmem_ld64(t_s, r);
+          tmem_ld_pair64<64>(t_s, r);
 #pragma unroll
           for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(r[i]);
         }
@@ -322,19 +294,18 @@ __global__ void __launch_bounds__(640, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[t]);
         ++ns;
-        const bool need_mask = (kv0 + 64 > S) || (args.causal && kv0 + 63 > q0);
-        if (need_mask) {
-          const int lim = args.causal ? min(S, qpos + 1) : S;
+        if (__any_sync(0xffffffffu, (kv0 + 64 > S) || (args.causal && kv0 + 63 > q0))) {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
             if (kv0 + i >= lim) s[i] = -INFINITY;
         }
         if (KMASK && mrow) {
-          key_mask_ballot<2>(kb);
-          if ((kb[0] & kb[1]) != 0xffffffffu) {
+          key_mask_ballot<4>(kb);
+          if ((kb[0] & kb[1] & kb[2] & kb[3]) != 0xffffffffu) {
+            const uint32_t k0 = c ? kb[2] : kb[0], k1 = c ? kb[3] : kb[1];
 #pragma unroll
             for (int i = 0; i < 64; ++i)
-              if (!((kb[i >> 5] >> (i & 31)) & 1u)) s[i] = -INFINITY;
+              if (!(((i < 32 ? k0 : k1) >> (i & 31)) & 1u)) s[i] = -INFINITY;
           }
         }
         float m8[8];
@@ -343,13 +314,7 @@ __global__ void __launch_bounds__(640, 1)
 #pragma unroll
         for (int i = 8; i < 32; ++i) m8[i & 7] = fmax3f(m8[i & 7], s[2 * i], s[2 * i + 1]);
         const float hm = fmax3f(fmax3f(m8[0], m8[1], m8[2]), fmax3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
-        // Exchange the half-row maxima (two slots by step parity: a warp is
-        // never more than one step ahead of its partner).
-        xm_own[(j & 1) * 32 + lane] = hm;
-        asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-        const float hp = xm_oth[(j & 1) * 32 + lane];
-        if (__any_sync(0xffffffffu, __float_as_uint(hp) == left_bits)) { ok = false; break; }
-        const float mx = fmaxf(hm, hp);
+        const float mx = fmaxf(hm, __shfl_xor_sync(0xffffffffu, hm, 16));
         const float m_cand = mx * sl2;
         float alpha = 1.f;
         bool rescale = false;
@@ -374,62 +339,45 @@ __global__ void __launch_bounds__(640, 1)
         const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
         l = l * alpha + ((a01.x + a01.y) + (a23.x + a23.y));
         if (np > 0) {
-          if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) {   // meets the partner's next exchange
-            xm_own[((j + 1) & 1) * 32 + lane] = __uint_as_float(left_bits);
-            xl_own[lane] = __uint_as_float(left_bits);
-            asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-            ok = false;
-            break;
-          }
+          if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
           tc_fence_after();
         }
-        if (j > 0 && o_mine && __any_sync(0xffffffffu, rescale)) {
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
           uint32_t r[OH];
-          if constexpr (OH == 32) tmem_ld32(t_o, *reinterpret_cast<uint32_t(*)[32]>(r));
-          else tmem_ld64(t_o, *reinterpret_cast<uint32_t(*)[64]>(r));
+          if constexpr (OH == 16) tmem_ld_pair16<16>(t_o, *reinterpret_cast<uint32_t(*)[16]>(r));
+          else tmem_ld_pair32<32>(t_o, *reinterpret_cast<uint32_t(*)[32]>(r));
 #pragma unroll
           for (int i = 0; i < OH; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          if constexpr (OH == 32) tmem_st32(t_o, *reinterpret_cast<uint32_t(*)[32]>(r));
-          else tmem_st64(t_o, *reinterpret_cast<uint32_t(*)[64]>(r));
+          if constexpr (OH == 16) tmem_st_pair16<16>(t_o, *reinterpret_cast<uint32_t(*)[16]>(r));
+          else tmem_st_pair32<32>(t_o, *reinterpret_cast<uint32_t(*)[32]>(r));
         }
-        tmem_st32(t_p, pk);
+        tmem_st_pair32<32>(t_p, pk);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
         ++np;
       }
       if (!ok) break;
-      // ---- epilogue: the two halves' row sums, then ctx = O / l (fp16). The
-      // pair barrier again carries a failure of either warp.
-      const bool fine_e = mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc);
-      xl_own[lane] = fine_e ? l : __uint_as_float(left_bits);
-      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-      const float lp = xl_oth[lane];
-      if (!fine_e || __any_sync(0xffffffffu, __float_as_uint(lp) == left_bits)) { ok = false; break; }
-      const float lt = l + lp;
+      // ---- epilogue: the two halves' row sums, then ctx = O / l (fp16).
+      if (!mbar_wait_warp(&pv_done[t], (np - 1) & 1, wc)) { ok = false; break; }
+      const float lt = l + __shfl_xor_sync(0xffffffffu, l, 16);
       tc_fence_after();
-      if (o_mine) {
-        const float inv_l = lt > 0.f ? 1.0f / lt : 0.f;
-        const int b = bh / args.H, h = bh % args.H;
+      const float inv_l = lt > 0.f ? 1.0f / lt : 0.f;
+      const int b = bh / args.H, h = bh % args.H;
+      uint32_t r[OH];
+      if constexpr (OH == 16) tmem_ld_pair16<16>(t_o, *reinterpret_cast<uint32_t(*)[16]>(r));
+      else tmem_ld_pair32<32>(t_o, *reinterpret_cast<uint32_t(*)[32]>(r));
+      if (qpos < S && ocol0 < args.dh) {
         __half* dst = args.ctx + ((long long)b * S + qpos) * args.d + (long long)h * args.dh + ocol0;
-#pragma unroll 1
-        for (int cc = 0; cc < OH / 32; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(t_o + cc * 32, r);
-          if (qpos < S && ocol0 + cc * 32 < args.dh) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              d4[v] = make_uint4(pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l),
-                                 pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l),
-                                 pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l),
-                                 pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l));
-            }
-          }
+        for (int v = 0; v < OH / 8; ++v) {
+          d4[v] = make_uint4(pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l),
+                             pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l),
+                             pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l),
+                             pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l));
         }
       }
-      // The next item's first exchange reuses xl / xm slots only after both
-      // warps have passed its named barrier, which they reach after this read.
       tc_fence_before();
     }
   }

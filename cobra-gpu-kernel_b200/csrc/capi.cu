@@ -284,17 +284,32 @@ int launch_gemm_tma_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
 template <int NC, int ST>
 int launch_gemm_ln_cluster_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const EpiArgs& ea, long long T,
                              int K, void* ws, cudaStream_t st) {
+  using Cfg = GemmLnClusterCfg<NC, ST>;
   auto kern = gemm_ln_cluster_kernel<NC, ST>;
-  const int smem = GemmLnClusterCfg<ST>::SMEM;
+  const int smem = Cfg::SMEM;
   int rc = ensure_smem((const void*)kern, smem);
   if (rc) return rc;
+  // x and y as [T, d] fp32 in 128B-swizzled boxes of 32 columns: 128 rows for
+  // the residual's chunks, one warp's 32 rows for the output's.
+  CUtensorMap map_x, map_y;
+  {
+    const unsigned long long dims[2] = {(unsigned long long)ea.d, (unsigned long long)T};
+    const unsigned long long strides[1] = {(unsigned long long)ea.d * 4};
+    const unsigned box_x[2] = {32, 128}, box_y[2] = {32, 32};
+    if ((rc = make_map(&map_x, ea.x, 2, dims, strides, box_x, CU_TENSOR_MAP_SWIZZLE_128B, "x",
+                       CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return rc;
+    if ((rc = make_map(&map_y, ea.y, 2, dims, strides, box_y, CU_TENSOR_MAP_SWIZZLE_128B, "y",
+                       CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+      return rc;
+  }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = NC;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -318,7 +333,7 @@ int launch_gemm_ln_cluster_t(const CUtensorMap& map_a, const CUtensorMap& map_b,
   const long long MT = (T + 127) / 128;
   const long long ncl = MT < max_clusters[dev] ? MT : max_clusters[dev];
   cfg.gridDim = dim3((unsigned)(ncl * NC), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, map_a, map_b, ea, T, K, reinterpret_cast<DevStatus*>(ws));
+  e = cudaLaunchKernelEx(&cfg, kern, map_a, map_b, map_x, map_y, ea, T, K, reinterpret_cast<DevStatus*>(ws));
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemm_ln_cluster_kernel)");
   return check_launch("gemm_ln_cluster_kernel");
 }
@@ -440,10 +455,10 @@ int run_outproj(const b200l_layer_desc* desc, const Plan& p, const float* x, flo
   // d = 256 NC: a cluster of NC CTAs shares each row tile and completes LN2 in
   // the epilogue (row statistics exchanged through distributed shared memory).
   switch (p.d) {
-    case 512: return launch_gemm_ln_cluster_t<2, 4>(map_a, map_b, ea, p.T, p.d, ws, st);
-    case 768: return launch_gemm_ln_cluster_t<3, 4>(map_a, map_b, ea, p.T, p.d, ws, st);
-    case 1024: return launch_gemm_ln_cluster_t<4, 4>(map_a, map_b, ea, p.T, p.d, ws, st);
-    case 1536: return launch_gemm_ln_cluster_t<6, 4>(map_a, map_b, ea, p.T, p.d, ws, st);
+    case 512: return launch_gemm_ln_cluster_t<2, 3>(map_a, map_b, ea, p.T, p.d, ws, st);
+    case 768: return launch_gemm_ln_cluster_t<3, 3>(map_a, map_b, ea, p.T, p.d, ws, st);
+    case 1024: return launch_gemm_ln_cluster_t<4, 3>(map_a, map_b, ea, p.T, p.d, ws, st);
+    case 1536: return launch_gemm_ln_cluster_t<6, 3>(map_a, map_b, ea, p.T, p.d, ws, st);
     case 2048: return launch_gemm_ln_cluster_t<8, 3>(map_a, map_b, ea, p.T, p.d, ws, st);
     default: break;
   }

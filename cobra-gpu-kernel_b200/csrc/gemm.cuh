@@ -618,47 +618,73 @@ __global__ void __launch_bounds__(192, 1)
 // for its 256 columns (written back to TMEM), its mean and the sum of squared
 // deviations about it (two passes over TMEM), stores that pair into every CTA
 // of the cluster (distributed shared memory) and arrives on each CTA's stats
-// barrier with cluster-scope release. After the
-// cluster-scope acquire, each thread combines the NC pairs (equal counts:
-// mean = average of the means, M2 = sum of M2 + 256 * sum of squared mean
-// offsets), normalises its 256 columns from TMEM and stores y. The residual
-// is added in fp32 before any rounding, as in EPI_RESID_LN (reference
-// _gemm_ln_kernel, torch_transformer_benchmark.py:394-463, which needs the
-// whole row in one tile; the reference's fallback for wider rows is a
-// separate _add_ln_kernel pass, :1289-1292 -- this kernel removes that pass).
+// barrier with cluster-scope release. After the cluster-scope acquire, each
+// thread combines the NC pairs (equal counts: mean = average of the means,
+// M2 = sum of M2 + 256 * sum of squared mean offsets), normalises its 256
+// columns from TMEM and stores y. The residual is added in fp32 before any
+// rounding, as in EPI_RESID_LN (reference _gemm_ln_kernel,
+// torch_transformer_benchmark.py:394-463, which needs the whole row in one
+// tile; the reference's fallback for wider rows is a separate _add_ln_kernel
+// pass, :1289-1292 -- this kernel removes that pass).
+//
+// The residual and the output move by TMA, in 32-column chunks of the tile
+// (128B-swizzled shared memory, so one thread per row reads and writes
+// 16-byte pieces without bank conflicts beyond the minimum):
+//   * warp 6 streams x chunks [128 rows x 32] into a two-chunk ring as soon
+//     as a slot frees -- x does not depend on the accumulator, so the next
+//     tile's first chunks land while this tile is still being normalised, and
+//     many bytes are in flight without holding registers;
+//   * each epilogue warp writes its 32 rows x 32 normalised columns into one
+//     of its two staging buffers and issues a TMA store of that box: full
+//     128-byte lines, rows past T clipped by the tensor map.
 // Every CTA of a cluster walks the same M tiles (cluster c: tiles c, c +
 // nclusters, ...), with the TMA producer and the MMA issuer running ahead
 // into the second TMEM accumulator. No TMA load uses cluster multicast: each
-// CTA loads its own A tile and its 256 rows of Wo.
+// CTA loads its own A tile, its 256 rows of Wo and its x columns.
+// Warps: 0 A / B producer, 1 MMA issuer + TMEM owner, 2-5 epilogue, 6 x producer.
 // ===========================================================================
-template <int ST>
+template <int NC, int ST>
 struct GemmLnClusterCfg {
   static constexpr int BN = 256;
   static constexpr int A_BYTES = 128 * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STATS_BYTES = 2 * 8 * 128 * 8;   // [slot][rank <= 8][row] (mean, M2)
-  static constexpr int SMEM = ST * STAGE + 256 + STATS_BYTES + 1024;
+  static constexpr int XS = 2;                          // x chunk ring slots
+  static constexpr int XCHUNK = 128 * 32 * 4;           // 128 rows x 32 fp32
+  static constexpr int YCHUNK = 32 * 32 * 4;            // one warp's 32 rows x 32 fp32
+  static constexpr int OFF_X = ST * STAGE;
+  static constexpr int OFF_Y = OFF_X + XS * XCHUNK;
+  static constexpr int OFF_BARS = OFF_Y + 4 * 2 * YCHUNK;
+  static constexpr int STATS_BYTES = 2 * NC * 128 * 8;  // [slot][rank][row] (mean, M2)
+  static constexpr int SMEM = OFF_BARS + 256 + STATS_BYTES + 1024;
+  static constexpr int THREADS = 224;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 template <int NC, int ST>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(224, 1)
     gemm_ln_cluster_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                           const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_y,
                            EpiArgs ea, long long T, int K, DevStatus* status) {
-  using C = GemmLnClusterCfg<ST>;
+  using C = GemmLnClusterCfg<NC, ST>;
   constexpr int BN = C::BN;
+  constexpr int XS = C::XS;
+  constexpr int NCH = BN / 32;   // 32-column chunks per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST * C::STAGE);
-  uint64_t* full = bars;                    // [ST]
-  uint64_t* empty = bars + ST;              // [ST]
-  uint64_t* acc_full = bars + 2 * ST;       // [2]
-  uint64_t* acc_empty = bars + 2 * ST + 2;  // [2], one arrival per epilogue warp
-  uint64_t* stats_full = bars + 2 * ST + 4; // [2], one arrival per epilogue thread of each CTA of the cluster
-  uint64_t* mma_done = bars + 2 * ST + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 7);
-  WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 2 * ST + 8);   // 2 slots
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BARS);
+  uint64_t* full = bars;                     // [ST]
+  uint64_t* empty = bars + ST;               // [ST]
+  uint64_t* acc_full = bars + 2 * ST;        // [2]
+  uint64_t* acc_empty = bars + 2 * ST + 2;   // [2], one arrival per epilogue warp
+  uint64_t* stats_full = bars + 2 * ST + 4;  // [2], one arrival per epilogue thread of each CTA of the cluster
+  uint64_t* x_full = bars + 2 * ST + 6;      // [XS]
+  uint64_t* x_empty = bars + 2 * ST + 8;     // [XS], one arrival per epilogue warp
+  uint64_t* mma_done = bars + 2 * ST + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 11);
+  WaitCtl* wc = reinterpret_cast<WaitCtl*>(bars + 2 * ST + 12);   // 2 slots
   float2* stats = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(bars) + 256);
+  uint8_t* xbuf = smem + C::OFF_X;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -677,11 +703,17 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&acc_empty[a], 4);
       mbar_init(&stats_full[a], NC * 128);
     }
+    for (int i = 0; i < XS; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 4);
+    }
     mbar_init(mma_done, 1);
     waitctl_init(wc, status);
     fence_barrier_init();
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
+    tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -741,13 +773,35 @@ __global__ void __launch_bounds__(192, 1)
       umma_commit(mma_done);
       mbar_drain(mma_done, 0);
     }
+  } else if (warp == 6) {
+    if (lane == 0) {  // ---- x producer: the residual's 32-column chunks, tile after tile
+      int last[XS];
+      for (int i = 0; i < XS; ++i) last[i] = -1;
+      long long g = 0;
+      bool ok = true;
+      for (long long mt = cid; mt < MT && ok; mt += ncl) {
+        for (int cc = 0; cc < NCH; ++cc, ++g) {
+          const int s = (int)(g % XS);
+          if (!mbar_wait(&x_empty[s], (uint32_t)((g / XS) & 1) ^ 1u, wc)) { ok = false; break; }
+          mbar_arrive_expect_tx(&x_full[s], C::XCHUNK);
+          tma_load_2d(xbuf + s * C::XCHUNK, &map_x, &x_full[s], n0 + cc * 32, (int)(mt * 128));
+          last[s] = (int)(g / XS);
+        }
+      }
+      for (int s = 0; s < XS; ++s)
+        if (last[s] >= 0) mbar_drain(&x_full[s], last[s] & 1);
+    }
   } else {  // ---- epilogue warps 2..5, one output row per thread
     const int qd = warp & 3;
     const int row = qd * 32 + lane;
     const int d = ea.d;
     const float inv_d = 1.0f / (float)d;
-    int ti = 0;
-    for (long long mt = cid; mt < MT; mt += ncl, ++ti) {
+    uint8_t* ystage = smem + C::OFF_Y + (warp - 2) * 2 * C::YCHUNK;
+    // 16-byte piece c of row r of a 128B-swizzled box sits at r * 128 + 16 * (c ^ (r & 7)).
+    const int xsw = row & 7, ysw = lane & 7;
+    int ti = 0, nstore = 0;
+    bool ok = true;
+    for (long long mt = cid; mt < MT && ok; mt += ncl, ++ti) {
       const int a = ti & 1;
       const long long t = mt * 128 + row;
       const bool valid = t < T;
@@ -755,28 +809,26 @@ __global__ void __launch_bounds__(192, 1)
       // y = LN2(x) there (BaselineSelfAttention, :121-122).
       const bool keep = ea.rowmask == nullptr || (valid && ea.rowmask[t] != 0);
       const uint32_t tl = tmem_base + a * BN + ((uint32_t)(qd * 32) << 16);
-      const float* xr = ea.x + t * d + n0;
       if (!mbar_wait_warp(&acc_full[a], (uint32_t)(ti >> 1) & 1, wc)) break;
       tc_fence_after();
       // pass 1: r = x + (acc + b) back into TMEM; row sum of these columns.
       float sum = 0.f;
-      float4 xn[8];
-      load_x_chunk(xr, 0, valid, BN, xn);
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        float4 xc[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) xc[c] = xn[c];
-        if (cc + 1 < BN / 32) load_x_chunk(xr, cc * 32 + 32, valid, BN, xn);
+      for (int cc = 0; cc < NCH; ++cc) {
+        const long long g = (long long)ti * NCH + cc;
+        const int s = (int)(g % XS);
+        if (!mbar_wait_warp(&x_full[s], (uint32_t)((g / XS) & 1), wc)) { ok = false; break; }
         uint32_t r[32];
         tmem_ld32(tl + cc * 32, r);
+        const uint8_t* xr = xbuf + s * C::XCHUNK + row * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
+          const float4 xv = *reinterpret_cast<const float4*>(xr + ((c ^ xsw) << 4));
           const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.bias + n0 + cc * 32) + c);
-          const float a0 = xc[c].x + (keep ? __uint_as_float(r[4 * c + 0]) + bv.x : 0.f);
-          const float a1 = xc[c].y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
-          const float a2 = xc[c].z + (keep ? __uint_as_float(r[4 * c + 2]) + bv.z : 0.f);
-          const float a3 = xc[c].w + (keep ? __uint_as_float(r[4 * c + 3]) + bv.w : 0.f);
+          const float a0 = xv.x + (keep ? __uint_as_float(r[4 * c + 0]) + bv.x : 0.f);
+          const float a1 = xv.y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
+          const float a2 = xv.z + (keep ? __uint_as_float(r[4 * c + 2]) + bv.z : 0.f);
+          const float a3 = xv.w + (keep ? __uint_as_float(r[4 * c + 3]) + bv.w : 0.f);
           sum += (a0 + a1) + (a2 + a3);
           r[4 * c + 0] = __float_as_uint(a0);
           r[4 * c + 1] = __float_as_uint(a1);
@@ -784,12 +836,18 @@ __global__ void __launch_bounds__(192, 1)
           r[4 * c + 3] = __float_as_uint(a3);
         }
         tmem_st32(tl + cc * 32, r);
+        // The chunk's reads (generic proxy) are done before TMA (async proxy)
+        // may refill the slot.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&x_empty[s]);
       }
+      if (!ok) break;
       const float mean_l = sum * (1.0f / (float)BN);
       // pass 2: squared deviations about this CTA's own mean.
       float m2 = 0.f;
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = 0; cc < NCH; ++cc) {
         uint32_t r[32];
         tmem_ld32(tl + cc * 32, r);
 #pragma unroll
@@ -803,7 +861,7 @@ __global__ void __launch_bounds__(192, 1)
       // that store) on each CTA's stats barrier, which expects one arrival
       // per epilogue thread of every CTA. Every wait stays bounded.
       const int slot = ti & 1;
-      const uint32_t my_entry = smem_u32(&stats[(slot * 8 + (int)rank) * 128 + row]);
+      const uint32_t my_entry = smem_u32(&stats[(slot * NC + (int)rank) * 128 + row]);
       const uint32_t bar_local = smem_u32(&stats_full[slot]);
 #pragma unroll 1
       for (int q = 0; q < NC; ++q) {
@@ -813,41 +871,50 @@ __global__ void __launch_bounds__(192, 1)
       if (!__all_sync(0xffffffffu, mbar_wait_cluster(&stats_full[slot], (uint32_t)(ti >> 1) & 1, wc))) break;
       float mean = 0.f;
 #pragma unroll
-      for (int q = 0; q < NC; ++q) mean += stats[(slot * 8 + q) * 128 + row].x;
+      for (int q = 0; q < NC; ++q) mean += stats[(slot * NC + q) * 128 + row].x;
       mean *= 1.0f / (float)NC;
       float M2 = 0.f;
 #pragma unroll
       for (int q = 0; q < NC; ++q) {
-        const float2 e = stats[(slot * 8 + q) * 128 + row];
+        const float2 e = stats[(slot * NC + q) * 128 + row];
         const float dm = e.x - mean;
         M2 += e.y + (float)BN * dm * dm;
       }
       const float rstd = rsqrtf(M2 * inv_d + ea.eps);
-      // pass 3: normalise this CTA's columns and store y.
+      // pass 3: normalise this CTA's columns into the warp's staging buffers
+      // and store each 32 x 32 box by TMA.
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = 0; cc < NCH; ++cc, ++nstore) {
         uint32_t r[32];
         tmem_ld32(tl + cc * 32, r);
-        if (valid) {
-          float* yr = ea.y + t * d + n0 + cc * 32;
+        uint8_t* yb = ystage + (nstore & 1) * C::YCHUNK;
+        if (lane == 0) bulk_wait_read<1>();   // the store that last used this buffer has read it
+        __syncwarp();
+        uint8_t* yr = yb + lane * 128;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int col = n0 + cc * 32 + 4 * c;
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(ea.ln_w + col));
-            const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.ln_b + col));
-            float4 o;
-            o.x = (__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bv.x;
-            o.y = (__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bv.y;
-            o.z = (__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bv.z;
-            o.w = (__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bv.w;
-            reinterpret_cast<float4*>(yr)[c] = o;
-          }
+        for (int c = 0; c < 8; ++c) {
+          const int col = n0 + cc * 32 + 4 * c;
+          const float4 wv = __ldg(reinterpret_cast<const float4*>(ea.ln_w + col));
+          const float4 bv = __ldg(reinterpret_cast<const float4*>(ea.ln_b + col));
+          float4 o;
+          o.x = (__uint_as_float(r[4 * c + 0]) - mean) * rstd * wv.x + bv.x;
+          o.y = (__uint_as_float(r[4 * c + 1]) - mean) * rstd * wv.y + bv.y;
+          o.z = (__uint_as_float(r[4 * c + 2]) - mean) * rstd * wv.z + bv.z;
+          o.w = (__uint_as_float(r[4 * c + 3]) - mean) * rstd * wv.w + bv.w;
+          *reinterpret_cast<float4*>(yr + ((c ^ ysw) << 4)) = o;
+        }
+        fence_proxy_async_smem();   // generic writes before the async-proxy (TMA) read
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_y, yb, n0 + cc * 32, (int)(mt * 128 + qd * 32));
+          bulk_commit();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
     }
+    if (lane == 0) bulk_wait_all();   // this warp's y stores are complete
   }
   __syncthreads();
   if (threadIdx.x == 0 && waitctl_aborted(wc)) record_error(status, kErrTimeout, kGemmTma, 10 + NC);
