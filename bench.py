@@ -109,6 +109,13 @@ def read_traffic(kernel: str, cfg_name: str):
     return None
 
 
+def workload_name(args, cfg) -> str:
+    """The config's name, marked when --batch / --heads changed its shape."""
+    base = CONFIGS[args.config]
+    mods = [f"{k}={cfg[k]}" for k in ("B", "H") if cfg[k] != base[k]]
+    return args.config if not mods else f"{args.config} ({', '.join(mods)})"
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -276,7 +283,7 @@ def run_reference_arm(args, cfg):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: x ~ N(0,1) fp32, seeded default nn.Linear init",
-            "config": {"workload": args.config, **cfg, "causal": False, "sample_note": r["sample"]},
+            "config": {"workload": workload_name(args, cfg), **cfg, "causal": False, "sample_note": r["sample"]},
             "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if "reference_layer" in r:
@@ -375,6 +382,9 @@ def main() -> int:
                     help="pieces per rank for the N > 1 scatter / gather (0: about 16 MiB each)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (smaller cases for ncu captures)")
+    ap.add_argument("--heads", type=int, default=0,
+                    help="override the config's head count (other head dims for ncu captures; "
+                         "the line then names a modified workload)")
     ap.add_argument("--model", default="layer", choices=["layer", "stack"],
                     help="layer: the judged single layer (default); stack: full blocks with the GELU FFN")
     ap.add_argument("--layers", type=int, default=2, help="--model stack: number of blocks")
@@ -384,6 +394,10 @@ def main() -> int:
     cfg = dict(CONFIGS[args.config])
     if args.batch > 0:
         cfg["B"] = args.batch
+    if args.heads > 0:
+        if cfg["d"] % args.heads or (cfg["d"] // args.heads) % 32:
+            raise SystemExit(f"--heads {args.heads}: d_model {cfg['d']} / heads must be a multiple of 32")
+        cfg["H"] = args.heads
 
     if args.impl == "reference":
         return run_reference_arm(args, cfg)
@@ -578,7 +592,7 @@ def main() -> int:
         "vs_baseline": None, "dtype": "fp16 operands / fp32 accumulate, fp32 in/out",
         "data": "synthetic: x ~ N(0,1) fp32 (sequence b drawn from a device generator seeded 101234+b), "
                 "seeded default nn.Linear init (seed 1234), no mask",
-        "config": {"workload": args.config, **cfg, "causal": False, "global_batch": B,
+        "config": {"workload": workload_name(args, cfg), **cfg, "causal": False, "global_batch": B,
                    "per_gpu_batch": -(-B // world),
                    "parallelism": f"batch shards over {world} GPU(s), no data-path collective",
                    "l2": "inputs larger than L2" if T * d * 4 > L2_BYTES else "inputs smaller than L2 (no flush)"},
