@@ -152,6 +152,10 @@ __global__ void __launch_bounds__(512, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // x is read twice (LN1, then the residual about two sequence pairs later):
+  // LN1's loads keep it in L2 (evict_last), the residual's TMA read and y's
+  // TMA store mark their lines evict_first, so the second read of x hits L2.
+  const uint64_t pol_keep = l2_policy_evict_last(), pol_once = l2_policy_evict_first();
 
   if (warp == 0) {
     if (lane == 0) {  // ======================= TMA producer: weight tiles
@@ -316,7 +320,7 @@ __global__ void __launch_bounds__(512, 1)
           const int r = r0 + 4 * it + grp;
 #pragma unroll
           for (int m = 0; m < NV; ++m)
-            v[it][m] = (r < S) ? ldg_stream_f4(a.x + (t0 + r) * DM + 32 * m + 4 * l8)
+            v[it][m] = (r < S) ? ldg_stream_f4_hint(a.x + (t0 + r) * DM + 32 * m + 4 * l8, pol_keep)
                                : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         float red[IT], mean[IT], rstd[IT];
@@ -585,7 +589,7 @@ __global__ void __launch_bounds__(512, 1)
       };
       if (leader) {
         mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
-        tma_load_3d(xbuf, &map_x, sb(s, FB_X0), 0, 0, seq);
+        tma_load_3d_hint(xbuf, &map_x, sb(s, FB_X0), 0, 0, seq, pol_once);
       }
       if (!mbar_wait_warp(sb(s, FB_OUT_FULL), pi & 1, wc)) break;
       tc_fence_after();
@@ -593,12 +597,12 @@ __global__ void __launch_bounds__(512, 1)
         for (int cc = 1; cc < NXC && cc < 3; ++cc) {
           uint64_t* bar = sb(s, cc == 1 ? FB_X1 : FB_X2);
           mbar_arrive_expect_tx(bar, 16384);
-          tma_load_3d(xchunk(cc), &map_x, bar, cc * 32, 0, seq);
+          tma_load_3d_hint(xchunk(cc), &map_x, bar, cc * 32, 0, seq, pol_once);
         }
         if constexpr (C::WO_STAGE) {
           if (mbar_wait(wo_done, pi & 1, wc)) {
             mbar_arrive_expect_tx(sb(s, FB_X3), 16384);
-            tma_load_3d(wbuf, &map_x, sb(s, FB_X3), 96, 0, seq);
+            tma_load_3d_hint(wbuf, &map_x, sb(s, FB_X3), 96, 0, seq, pol_once);
           }
         }
       }
@@ -699,12 +703,12 @@ __global__ void __launch_bounds__(512, 1)
           // chunk 3 (the weight buffer), chunk 0 (k|v, the next sequence's
           // first epilogue), chunks 1-2 (ctx, after its first softmax).
           if constexpr (C::WO_STAGE) {
-            tma_store_3d(&map_y, wbuf, 96, 0, seq);
+            tma_store_3d_hint(&map_y, wbuf, 96, 0, seq, pol_once);
             bulk_commit();
           }
-          tma_store_3d(&map_y, xchunk(0), 0, 0, seq);
+          tma_store_3d_hint(&map_y, xchunk(0), 0, 0, seq, pol_once);
           bulk_commit();
-          for (int cc = 1; cc < NXC && cc < 3; ++cc) tma_store_3d(&map_y, xchunk(cc), cc * 32, 0, seq);
+          for (int cc = 1; cc < NXC && cc < 3; ++cc) tma_store_3d_hint(&map_y, xchunk(cc), cc * 32, 0, seq, pol_once);
           bulk_commit();
           if constexpr (C::WO_STAGE) {
             bulk_wait_read<2>();

@@ -616,7 +616,8 @@ __global__ void __launch_bounds__(192, 1)
 // CTAs shares each 128-row M tile, CTA rank r owning output columns
 // [256 r, 256 r + 256). Each epilogue thread (one row) forms r = x + acc + bo
 // for its 256 columns (written back to TMEM), its mean and the sum of squared
-// deviations about it (two passes over TMEM), stores that pair into every CTA
+// deviations about it (one pass: sums of the differences from the row's first
+// value here and of their squares), stores that pair into every CTA
 // of the cluster (distributed shared memory) and arrives on each CTA's stats
 // barrier with cluster-scope release. After the cluster-scope acquire, each
 // thread combines the NC pairs (equal counts: mean = average of the means,
@@ -811,8 +812,10 @@ __global__ void __launch_bounds__(224, 1)
       const uint32_t tl = tmem_base + a * BN + ((uint32_t)(qd * 32) << 16);
       if (!mbar_wait_warp(&acc_full[a], (uint32_t)(ti >> 1) & 1, wc)) break;
       tc_fence_after();
-      // pass 1: r = x + (acc + b) back into TMEM; row sum of these columns.
-      float sum = 0.f;
+      // pass 1: r = x + (acc + b) back into TMEM, with the sums of (r - K) and
+      // (r - K)^2 about the row's first value K here (a shift inside the
+      // row's range keeps the one-pass variance free of cancellation).
+      float s1 = 0.f, s2 = 0.f, shift = 0.f;
 #pragma unroll 1
       for (int cc = 0; cc < NCH; ++cc) {
         const long long g = (long long)ti * NCH + cc;
@@ -829,33 +832,25 @@ __global__ void __launch_bounds__(224, 1)
           const float a1 = xv.y + (keep ? __uint_as_float(r[4 * c + 1]) + bv.y : 0.f);
           const float a2 = xv.z + (keep ? __uint_as_float(r[4 * c + 2]) + bv.z : 0.f);
           const float a3 = xv.w + (keep ? __uint_as_float(r[4 * c + 3]) + bv.w : 0.f);
-          sum += (a0 + a1) + (a2 + a3);
+          if (cc == 0 && c == 0) shift = a0;
+          const float d0 = a0 - shift, d1 = a1 - shift, d2 = a2 - shift, d3 = a3 - shift;
+          s1 += (d0 + d1) + (d2 + d3);
+          s2 += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
           r[4 * c + 0] = __float_as_uint(a0);
           r[4 * c + 1] = __float_as_uint(a1);
           r[4 * c + 2] = __float_as_uint(a2);
           r[4 * c + 3] = __float_as_uint(a3);
         }
         tmem_st32(tl + cc * 32, r);
-        // The chunk's reads (generic proxy) are done before TMA (async proxy)
-        // may refill the slot.
-        fence_proxy_async_smem();
+        // The chunk's values were consumed (tmem_st32 waited for them) before
+        // this release, so TMA may refill the slot.
         __syncwarp();
         if (lane == 0) mbar_arrive(&x_empty[s]);
       }
       if (!ok) break;
-      const float mean_l = sum * (1.0f / (float)BN);
-      // pass 2: squared deviations about this CTA's own mean.
-      float m2 = 0.f;
-#pragma unroll 1
-      for (int cc = 0; cc < NCH; ++cc) {
-        uint32_t r[32];
-        tmem_ld32(tl + cc * 32, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float dv = __uint_as_float(r[i]) - mean_l;
-          m2 += dv * dv;
-        }
-      }
+      const float dmean = s1 * (1.0f / (float)BN);
+      const float mean_l = shift + dmean;
+      const float m2 = fmaxf(s2 - s1 * dmean, 0.f);   // squared deviations about mean_l
       // Exchange (mean, M2) of this row with every CTA of the cluster: store
       // the pair into each CTA's slot, then arrive (cluster-scope release of
       // that store) on each CTA's stats barrier, which expects one arrival
