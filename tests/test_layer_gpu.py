@@ -26,7 +26,8 @@ pytestmark = pytest.mark.gpu
 
 # (B, S, d, H, causal) -- covers every kernel template:
 # K1 KP in {64,128,192,256} + the d>256 TMA path; K2 dhp in {32,64,128,256};
-# K3 BN in {64,128,192,256} + the d>256 residual path.
+# K3 BN in {64,128,192,256}, the clusters for d = 256 NC (NC 2, 3, 4, 6, 8)
+# and the d>256 residual path.
 SHAPES = [
     (4, 128, 128, 4, False),     # cfg1
     (3, 17, 96, 3, False),       # odd shape (tools/validate.py:96-97)
@@ -35,6 +36,10 @@ SHAPES = [
     (2, 96, 256, 1, False),      # dh 256
     (2, 70, 160, 5, False),      # d 160 -> KP 192
     (2, 200, 512, 4, False),     # dh 128, d > 256 path
+    (2, 150, 768, 6, False),     # K3 cluster of 3 CTAs, last row tile partial
+    (1, 130, 1536, 12, False),   # K3 cluster of 6
+    (1, 140, 2048, 16, False),   # K3 cluster of 8
+    (2, 100, 640, 5, False),     # d > 256 but not 256 * NC: residual epilogue + row LayerNorm
     (1, 160, 1024, 16, False),   # cfg5 family, short S
     (2, 300, 128, 4, True),      # causal, 3 query tiles
     (1, 1, 128, 4, False),       # S = 1 (tools/validate.py:94-95)
