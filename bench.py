@@ -586,6 +586,15 @@ def main() -> int:
         if "reference_layer" in c:
             cpu["reference_layer"] = c["reference_layer"]
 
+    if roof is not None and roof["kernel"] == "flash_attn" and clocks and clocks.get("sm_mhz"):
+        # Exponential-bound ceiling of the attention kernel: one MUFU ex2 per
+        # score (16 per clock per SM) against 4 * head_dim tensor FLOPs per
+        # score, at the SM clock sampled during the timed steps.
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        ceil = 16.0 * sms * clocks["sm_mhz"] * 1e6 * 4.0 * (d // cfg["H"]) / 1e12
+        roof["exp_bound"] = {"ceiling_tflops": ceil, "frac": roof["achieved"] / ceil, "sm_mhz": clocks["sm_mhz"],
+                             "basis": f"16 ex2/clk/SM x {sms} SMs x 4*head_dim FLOP per score"}
+
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
