@@ -265,16 +265,19 @@ int launch_qkv_lnfused_t(const b200l_layer_desc* desc, const Plan& p, const floa
 
 template <int BN, int ST, int EPI>
 int launch_gemm_tma_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const EpiArgs& ea, long long T, int K, int N,
-                      void* ws, cudaStream_t st) {
+                      void* ws, cudaStream_t st, const QkvMaps* qm = nullptr) {
   auto kern = gemm_tma_kernel<BN, ST, EPI>;
-  const int smem = GemmTmaCfg<BN, ST>::SMEM;
+  const int smem = EPI == EPI_QKV ? GemmTmaCfg<BN, ST>::SMEM_QKV : GemmTmaCfg<BN, ST>::SMEM;
+  QkvMaps maps;
+  if (qm) maps = *qm;
+  else memset(&maps, 0, sizeof maps);
   int rc = ensure_smem((const void*)kern, smem);
   if (rc) return rc;
   DevInfo dev;
   if ((rc = device_info(&dev))) return rc;
   const long long tiles = ((T + 127) / 128) * ((N + BN - 1) / BN);   // persistent: at most one CTA per SM
   const unsigned grid = (unsigned)(tiles < dev.sms ? tiles : dev.sms);
-  kern<<<grid, 192, smem, st>>>(map_a, map_b, ea, T, K, N, reinterpret_cast<DevStatus*>(ws));
+  kern<<<grid, 192, smem, st>>>(map_a, map_b, maps, ea, T, K, N, reinterpret_cast<DevStatus*>(ws));
   return check_launch("gemm_tma_kernel");
 }
 
@@ -359,10 +362,26 @@ int run_qkv(const b200l_layer_desc* desc, const Plan& p, const float* x, void* w
   ea.qkv = qkv_out(p, ws);
   ea.bias = desc->bqkv;
   ea.d = p.d;
-  // Three stages (144 KB): the q / k / v^T scatter epilogue, not the operand
-  // ring, bounds this GEMM (without its stores it ran 26 % faster), and with
-  // four stages it measured 4 % slower.
-  return launch_gemm_tma_t<256, 3, EPI_QKV>(map_a, map_b, ea, p.T, p.d, 3 * p.dq, ws, st);
+  // q, k [B*Hl, S, dhp] and v^T [B*Hl, dhp, sp] in 32 x 32 boxes (64-byte
+  // swizzle) for the epilogue's TMA stores.
+  QkvMaps qm;
+  memset(&qm, 0, sizeof qm);
+  {
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    const unsigned long long bh = (unsigned long long)p.B * p.Hl;
+    const unsigned long long dq[3] = {(unsigned long long)p.dhp, (unsigned long long)p.S, bh};
+    const unsigned long long sq[2] = {(unsigned long long)p.dhp * 2, (unsigned long long)p.S * p.dhp * 2};
+    const unsigned long long dv[3] = {(unsigned long long)p.sp, (unsigned long long)p.dhp, bh};
+    const unsigned long long sv[2] = {(unsigned long long)p.sp * 2, (unsigned long long)p.dhp * p.sp * 2};
+    const unsigned box[3] = {32, 32, 1};
+    if ((rc = make_map(&qm.q, w + p.off_q, 3, dq, sq, box, CU_TENSOR_MAP_SWIZZLE_64B, "q box"))) return rc;
+    if ((rc = make_map(&qm.k, w + p.off_k, 3, dq, sq, box, CU_TENSOR_MAP_SWIZZLE_64B, "k box"))) return rc;
+    if ((rc = make_map(&qm.vt, w + p.off_vt, 3, dv, sv, box, CU_TENSOR_MAP_SWIZZLE_64B, "v^T box"))) return rc;
+    qm.use = 1;
+  }
+  // Three stages (144 KB) of the operand ring; with four stages it measured
+  // 4 % slower.
+  return launch_gemm_tma_t<256, 3, EPI_QKV>(map_a, map_b, ea, p.T, p.d, 3 * p.dq, ws, st, &qm);
 }
 
 // TWO_TILE: the two-query-tile kernel with P in TMEM (head_dim <= 64);

@@ -27,6 +27,14 @@ struct QkvOut {
   int dq;   // width of each of the q / k / v projections: H * dh (the heads computed)
 };
 
+// Tensor maps of the q, k (fp16 [B*H, S, dhp]) and v^T (fp16 [B*H, dhp, sp])
+// outputs in 32 x 32 boxes with the 64-byte swizzle, for the QKV epilogue's
+// TMA stores; `use` is 0 when they are not set (the per-thread stores run).
+struct alignas(64) QkvMaps {
+  CUtensorMap q, k, vt;
+  int use;
+};
+
 // Stores 32 consecutive projection columns [col0, col0+32) of token t.
 // dh is a multiple of 32, so the chunk lies inside one (q|k|v, head) block.
 __device__ __forceinline__ void qkv_store_chunk(const QkvOut& o, const float* __restrict__ bqkv, long long t,
@@ -325,6 +333,8 @@ struct GemmTmaCfg {
   static constexpr int B_BYTES = BN * 128;   // BN rows x 64 fp16
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int SMEM = ST * STAGE + 256 + 1024;
+  static constexpr int QKV_STAGE = 4 * 2 * 2048;       // EPI_QKV: two 32 x 32 fp16 boxes per epilogue warp
+  static constexpr int SMEM_QKV = ST * STAGE + 1024 + QKV_STAGE + 1024;
   static constexpr int ACC_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
   static constexpr int NACC = 2 * ACC_COLS <= 512 ? 2 : 1;      // TMEM accumulators
   static constexpr int TMEM_COLS = NACC * ACC_COLS;
@@ -333,7 +343,7 @@ struct GemmTmaCfg {
 template <int BN, int ST, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                    EpiArgs ea, long long T, int K, int N, DevStatus* status) {
+                    const __grid_constant__ QkvMaps qm, EpiArgs ea, long long T, int K, int N, DevStatus* status) {
   using C = GemmTmaCfg<BN, ST>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -432,6 +442,8 @@ __global__ void __launch_bounds__(192, 1)
     const int qd = warp & 3;
     const int row = qd * 32 + lane;
     int ti = 0;
+    uint8_t* qstage = smem + ST * C::STAGE + 1024 + (warp - 2) * 4096;   // EPI_QKV staging
+    int nqst = 0;
     float4 xn[8];          // EPI_RESID_LN: the next x chunk of this thread's row, loaded ahead
     bool x_next = false;   // xn already holds the first chunk of this tile's row
     for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
@@ -452,13 +464,64 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait_warp(&acc_full[a], (uint32_t)(ti / C::NACC) & 1, wc)) break;
       tc_fence_after();
       if constexpr (EPI == EPI_QKV) {
+        // A warp whose 32 rows lie in one sequence stores each 32-column chunk
+        // as one 32 x 32 box by TMA (q / k rows, or the transposed v^T block),
+        // staged through 64-byte-swizzled shared memory; other warps (a
+        // sequence boundary inside the rows, rows past T, padded head_dim)
+        // store per thread.
+        const QkvOut& o = ea.qkv;
+        const long long r0 = m0 + qd * 32;
+        const long long b0 = r0 / o.S;
+        const int s0 = (int)(r0 - b0 * o.S);
+        const bool box_ok = qm.use && r0 + 31 < T && s0 + 31 < o.S && o.dh == o.dhp;
 #pragma unroll 1
         for (int cc = 0; cc < BN / 32; ++cc) {
           const int col0 = n0 + cc * 32;
           if (col0 >= N) break;
           uint32_t r[32];
           tmem_ld32(tl + cc * 32, r);
-          if (valid) qkv_store_chunk(ea.qkv, ea.bias, t, col0, r);
+          const int which = col0 / o.dq;
+          if (!box_ok || (which == 2 && (s0 & 7) != 0)) {   // v^T boxes start on a 16-byte column
+            if (valid) qkv_store_chunk(o, ea.bias, t, col0, r);
+            continue;
+          }
+          const int within = col0 - which * o.dq;
+          const int head = within / o.dh;
+          const int j0 = within - head * o.dh;
+          const int bh = (int)(b0 * o.H + head);
+          uint8_t* yb = qstage + (nqst & 1) * 2048;
+          ++nqst;
+          if (lane == 0) bulk_wait_read<1>();   // the store that last used this buffer has read it
+          __syncwarp();
+          const uint32_t ys = smem_u32(yb);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {   // bqkv is 16-byte aligned (checked on the host)
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(ea.bias + col0) + i);
+            pk[2 * i] = pack_half2(__uint_as_float(r[4 * i + 0]) + b4.x, __uint_as_float(r[4 * i + 1]) + b4.y);
+            pk[2 * i + 1] = pack_half2(__uint_as_float(r[4 * i + 2]) + b4.z, __uint_as_float(r[4 * i + 3]) + b4.w);
+          }
+          if (which < 2) {   // this lane's row: four 16-byte pieces
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              st_shared_v4(ys + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                           pk[4 * c + 3]);
+          } else {           // this lane's token is column `lane` of the 32 (head_dim) x 32 (token) box
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+              const uint32_t w = pk[jj >> 1];
+              st_shared_u16(ys + jj * 64 + (((lane >> 3) ^ ((jj >> 1) & 3)) << 4) + (lane & 7) * 2,
+                            (unsigned short)((jj & 1) ? (w >> 16) : (w & 0xffffu)));
+            }
+          }
+          fence_proxy_async_smem();   // generic writes before the async-proxy (TMA) read
+          __syncwarp();
+          if (lane == 0) {
+            if (which == 0) tma_store_3d(&qm.q, yb, j0, s0, bh);
+            else if (which == 1) tma_store_3d(&qm.k, yb, j0, s0, bh);
+            else tma_store_3d(&qm.vt, yb, s0, j0, bh);
+            bulk_commit();
+          }
         }
       } else if constexpr (EPI == EPI_RESID) {
 #pragma unroll 1
@@ -598,6 +661,9 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+    if constexpr (EPI == EPI_QKV) {
+      if (lane == 0) bulk_wait_all();   // this warp's q / k / v^T box stores are complete
     }
   }
   __syncthreads();
