@@ -54,6 +54,7 @@ template <int DHP, int BN, bool KMASK>   // KMASK: a key-padding mask may be giv
 __global__ void __launch_bounds__(192, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_vt, AttnArgs args, DevStatus* status) {
+  pdl_wait_then_release();
   using C = AttnCfg<DHP, BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

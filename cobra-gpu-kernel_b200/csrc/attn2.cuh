@@ -68,6 +68,7 @@ template <int DHP, bool KMASK>   // KMASK: a key-padding mask may be given
 __global__ void __launch_bounds__(640, 1)
     attn2_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                  const __grid_constant__ CUtensorMap map_vt, AttnArgs args, DevStatus* status) {
+  pdl_wait_then_release();
   using C = Attn2Cfg<DHP>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];

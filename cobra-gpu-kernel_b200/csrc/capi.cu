@@ -231,11 +231,32 @@ int check_launch(const char* what) {
 }
 
 // ---------------------------------------------------------------- launches
+// Launch with programmatic stream serialisation: the grid may be scheduled
+// while the previous kernel on the stream finishes; every layer kernel starts
+// with griddepcontrol.wait (pdl_wait_then_release), so none of its work runs
+// before its predecessor has completed.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <int VPL, bool F16>
 int launch_row_ln_t(const float* in, void* out, const float* w, const float* b, float eps, long long T, int d,
                     cudaStream_t st, const uint8_t* rowmask) {
   const long long blocks = (T + 7) / 8;
-  row_ln_kernel<VPL, F16><<<(unsigned)blocks, 256, 0, st>>>(in, out, w, b, eps, T, d, rowmask);
+  cudaError_t e = launch_pdl(row_ln_kernel<VPL, F16>, dim3((unsigned)blocks), dim3(256), 0, st, in, out, w, b, eps, T, d,
+                             rowmask);
+  if (e != cudaSuccess) return cuda_fail(e, "row_ln_kernel");
   return check_launch("row_ln_kernel");
 }
 template <bool F16>
@@ -258,8 +279,10 @@ int launch_qkv_lnfused_t(const b200l_layer_desc* desc, const Plan& p, const floa
   const int smem = QkvLnFusedCfg<KP>::SMEM;
   if ((rc = ensure_smem((const void*)kern, smem))) return rc;
   const long long blocks = (p.T + 127) / 128;
-  kern<<<(unsigned)blocks, 256, smem, st>>>(map_w, x, desc->ln1_w, desc->ln1_b, desc->eps1, desc->bqkv, qkv_out(p, ws),
-                                            p.T, p.d, 3 * p.dq, reinterpret_cast<DevStatus*>(ws));
+  cudaError_t e = launch_pdl(kern, dim3((unsigned)blocks), dim3(256), smem, st, map_w, x, desc->ln1_w, desc->ln1_b,
+                             desc->eps1, desc->bqkv, qkv_out(p, ws), p.T, p.d, 3 * p.dq,
+                             reinterpret_cast<DevStatus*>(ws));
+  if (e != cudaSuccess) return cuda_fail(e, "qkv_lnfused_kernel");
   return check_launch("qkv_lnfused_kernel");
 }
 
@@ -277,7 +300,9 @@ int launch_gemm_tma_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
   if ((rc = device_info(&dev))) return rc;
   const long long tiles = ((T + 127) / 128) * ((N + BN - 1) / BN);   // persistent: at most one CTA per SM
   const unsigned grid = (unsigned)(tiles < dev.sms ? tiles : dev.sms);
-  kern<<<grid, 192, smem, st>>>(map_a, map_b, maps, ea, T, K, N, reinterpret_cast<DevStatus*>(ws));
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(192), smem, st, map_a, map_b, maps, ea, T, K, N,
+                             reinterpret_cast<DevStatus*>(ws));
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_tma_kernel");
   return check_launch("gemm_tma_kernel");
 }
 
@@ -307,16 +332,18 @@ int launch_gemm_ln_cluster_t(const CUtensorMap& map_a, const CUtensorMap& map_b,
       return rc;
   }
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = NC;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see launch_pdl
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   static int max_clusters[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -326,8 +353,10 @@ int launch_gemm_ln_cluster_t(const CUtensorMap& map_a, const CUtensorMap& map_b,
     std::lock_guard<std::mutex> lk(g_mu);
     if (max_clusters[dev] == 0) {
       cfg.gridDim = dim3(NC * 16, 1, 1);
+      cfg.numAttrs = 1;   // the occupancy query sees the cluster shape only
       int n = 0;
       e = cudaOccupancyMaxActiveClusters(&n, (const void*)kern, &cfg);
+      cfg.numAttrs = 2;
       if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
       if (n <= 0) return fail(B200L_ERR_LAUNCH, "no cluster of %d CTAs fits on this device", NC);
       max_clusters[dev] = n;
@@ -423,7 +452,9 @@ int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& de
     if (rc) return rc;
     const long long items = (long long)BH * ((p.S + 255) / 256);
     const int grid = items < dev.sms ? (int)items : dev.sms;
-    kern<<<grid, Attn2Cfg<DHP>::THREADS, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
+    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(Attn2Cfg<DHP>::THREADS), smem, st, mq, mk, mv, a,
+                               reinterpret_cast<DevStatus*>(ws));
+    if (e != cudaSuccess) return cuda_fail(e, "attn2_kernel");
     return check_launch("attn2_kernel");
   } else {
     auto kern = a.kmask ? attn_kernel<DHP, BN, true> : attn_kernel<DHP, BN, false>;
@@ -431,7 +462,8 @@ int launch_attn_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& de
     int rc = ensure_smem((const void*)kern, smem);
     if (rc) return rc;
     const int grid = a.num_items < dev.sms ? a.num_items : dev.sms;
-    kern<<<grid, 192, smem, st>>>(mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
+    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(192), smem, st, mq, mk, mv, a, reinterpret_cast<DevStatus*>(ws));
+    if (e != cudaSuccess) return cuda_fail(e, "attn_kernel");
     return check_launch("attn_kernel");
   }
 }

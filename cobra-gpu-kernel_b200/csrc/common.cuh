@@ -66,6 +66,17 @@ __device__ __forceinline__ bool waitctl_aborted(const WaitCtl* wc) {
   return *reinterpret_cast<const volatile int*>(&wc->abort) != 0;
 }
 
+// Programmatic dependent launch. The layer kernels are launched with
+// programmatic stream serialisation, so a kernel's grid can be scheduled while
+// its predecessor on the stream is still finishing; each of them waits here,
+// first thing, for the predecessor grid to complete and its memory to be
+// visible (a no-op when launched without the attribute), then lets its own
+// dependent be scheduled.
+__device__ __forceinline__ void pdl_wait_then_release() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(256, 1)
     qkv_lnfused_kernel(const __grid_constant__ CUtensorMap map_w, const float* __restrict__ x,
                        const float* __restrict__ ln_w, const float* __restrict__ ln_b, float eps,
                        const float* __restrict__ bqkv, QkvOut out, long long T, int d, int N, DevStatus* status) {
+  pdl_wait_then_release();
   using C = QkvLnFusedCfg<KP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -344,6 +345,7 @@ template <int BN, int ST, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const __grid_constant__ QkvMaps qm, EpiArgs ea, long long T, int K, int N, DevStatus* status) {
+  pdl_wait_then_release();
   using C = GemmTmaCfg<BN, ST>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -733,6 +735,7 @@ __global__ void __launch_bounds__(224, 1)
     gemm_ln_cluster_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                            const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_y,
                            EpiArgs ea, long long T, int K, DevStatus* status) {
+  pdl_wait_then_release();
   using C = GemmLnClusterCfg<NC, ST>;
   constexpr int BN = C::BN;
   constexpr int XS = C::XS;

@@ -23,6 +23,7 @@ __global__ void __launch_bounds__(256) row_ln_kernel(const float* __restrict__ i
                                                      const float* __restrict__ w, const float* __restrict__ b,
                                                      float eps, long long T, int d,
                                                      const uint8_t* __restrict__ rowmask) {
+  pdl_wait_then_release();
   const int warps = blockDim.x >> 5;
   const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
