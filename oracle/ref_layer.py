@@ -230,7 +230,7 @@ def streamed_keys(layer: ReferenceLayer, xs: torch.Tensor, dtype: torch.dtype = 
 
 
 def streamed_ctx_rows(layer: ReferenceLayer, h: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                      rows: torch.Tensor, causal: bool) -> torch.Tensor:
+                      rows: torch.Tensor, causal: bool, key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Second phase: ctx rows [R, d] for the query positions ``rows``.
 
     Follows ``chunked_attention`` (tools/reference_chunked.py:73-128): each
@@ -238,7 +238,9 @@ def streamed_ctx_rows(layer: ReferenceLayer, h: torch.Tensor, k: torch.Tensor, v
     axis is never blocked, so the softmax normalisation is exact), causal
     keys are masked with -inf before the softmax (:109-113), and
     ctx = probs @ v (:120). Only the sampled query rows are formed, so memory
-    is O(R * S) per head. Computed in the dtype of h / k / v.
+    is O(R * S) per head. Computed in the dtype of h / k / v. ``key_mask``
+    (bool [S], True = valid token) gives padded keys -inf scores, as
+    BaselineSelfAttention does (torch_transformer_benchmark.py:106-109).
     """
     att = layer.attention
     H, dh = att.num_heads, att.head_dim
@@ -253,6 +255,8 @@ def streamed_ctx_rows(layer: ReferenceLayer, h: torch.Tensor, k: torch.Tensor, v
         if causal:
             kpos = torch.arange(S)[None, :]
             sc = sc.masked_fill(kpos > rows[:, None], float("-inf"))
+        if key_mask is not None:
+            sc = sc.masked_fill(~key_mask[None, :], float("-inf"))
         p = torch.softmax(sc, dim=-1)
         ctx[:, sl] = p @ v[:, sl]
         del sc, p
@@ -260,31 +264,38 @@ def streamed_ctx_rows(layer: ReferenceLayer, h: torch.Tensor, k: torch.Tensor, v
 
 
 def streamed_output_rows(layer: ReferenceLayer, xs: torch.Tensor, ctx: torch.Tensor,
-                         rows: torch.Tensor) -> torch.Tensor:
-    """Last phase: y rows = LN2(x + ctx Wo^T + bo) (:119, :141, :131), in ctx's dtype."""
+                         rows: torch.Tensor, key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Last phase: y rows = LN2(x + ctx Wo^T + bo) (:119, :141, :131), in ctx's
+    dtype; a padded query row's attention output is zeroed, bias included
+    (:121-122), so its y is LN2(x)."""
     att = layer.attention
     f = lambda t: t.detach().to(ctx.dtype)
-    r = f(xs[rows]) + ctx @ f(att.out_proj.weight).T + f(att.out_proj.bias)
+    out = ctx @ f(att.out_proj.weight).T + f(att.out_proj.bias)
+    if key_mask is not None:
+        out = out.masked_fill(~key_mask[rows][:, None], 0)
+    r = f(xs[rows]) + out
     return _ln64(r, f(layer.norm2.weight), f(layer.norm2.bias), layer.norm2.eps)
 
 
 def _attn_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor, rows: torch.Tensor,
-                    causal: bool) -> torch.Tensor:
+                    causal: bool, key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
     """ctx rows [R, d] in fp64 for one sequence ``xs`` [S, d] (streamed_keys,
     then streamed_ctx_rows)."""
     h, k, v = streamed_keys(layer, xs, torch.float64)
-    return streamed_ctx_rows(layer, h, k, v, rows, causal)
+    return streamed_ctx_rows(layer, h, k, v, rows, causal, key_mask)
 
 
 def streamed_attention_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor,
-                                 rows: Sequence[int], causal: bool = False) -> torch.Tensor:
+                                 rows: Sequence[int], causal: bool = False,
+                                 key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
     """fp64 attention context (before out_proj) for sampled query rows of one sequence."""
     rows_t = torch.as_tensor(rows, dtype=torch.long)
-    return _attn_rows_fp64(layer, xs, rows_t, causal)
+    return _attn_rows_fp64(layer, xs, rows_t, causal, key_mask)
 
 
 def streamed_layer_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor,
-                             rows: Sequence[int], causal: bool = False) -> torch.Tensor:
+                             rows: Sequence[int], causal: bool = False,
+                             key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
     """fp64 layer output y for sampled query rows of one sequence ``xs`` [S, d].
 
     This is the long-context oracle: ``BaselineSelfAttention`` would
@@ -292,8 +303,8 @@ def streamed_layer_rows_fp64(layer: ReferenceLayer, xs: torch.Tensor,
     infeasible at S=100000, so the layer is restated per sampled row in fp64.
     """
     rows_t = torch.as_tensor(rows, dtype=torch.long)
-    ctx = _attn_rows_fp64(layer, xs, rows_t, causal)
-    return streamed_output_rows(layer, xs, ctx, rows_t)
+    ctx = _attn_rows_fp64(layer, xs, rows_t, causal, key_mask)
+    return streamed_output_rows(layer, xs, ctx, rows_t, key_mask)
 
 
 def sample_rows(seq_len: int, count: int, seed: int) -> torch.Tensor:

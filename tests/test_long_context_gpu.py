@@ -53,6 +53,34 @@ def test_cfg5_sampled_rows_fp64(pkg, cuda_ok, causal):
         assert rel < 1e-2, f"sequence {b}: ctx max error {rel:.3e} of max |ctx|"
 
 
+def test_cfg5_key_mask_sampled_rows_fp64(pkg, cuda_ok):
+    """cfg5 shape with a key-padding mask (the masked long-context kernel):
+    sequence 0 padded after 61234 tokens, sequence 1 with 30 % of its tokens
+    scattered invalid. Sampled rows, valid and padded, against the fp64
+    streamed oracle given the same mask (padded keys get no probability,
+    padded rows y = LN2(x))."""
+    B, S, d, H = 2, 100000, 1024, 16
+    cfg = TransformerConfig(B, S, d, H)
+    ref = build_reference_layer(cfg, 1234)
+    lay = pkg.B200TransformerLayer(d, H, use_graphs=False).cuda().eval()
+    lay.load_state_dict(ref.state_dict(), strict=True)
+    x, _ = generate_random_case(cfg, seed=4321)
+    g = torch.Generator().manual_seed(77)
+    mask = torch.stack([torch.arange(S) < 61234, torch.rand(S, generator=g) > 0.3])
+    with torch.inference_mode():
+        y = lay(x.cuda(), mask.cuda())
+        torch.cuda.synchronize()
+        lay.check_status()
+        y = y.cpu()
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    for b in range(B):
+        rows = torch.unique(torch.cat([sample_rows(S, 200, seed=2000 + b),
+                                       torch.tensor([0, 61233, 61234, 61235, 99999])]))
+        y_ref = streamed_layer_rows_fp64(ref, x[b], rows, False, key_mask=mask[b])
+        res = compare_outputs(y_ref, y[b, rows])
+        assert res.passed, f"sequence {b}: {res}"
+
+
 def test_cfg5_full_batch_one_launch(pkg, cuda_ok):
     """cfg5 exactly as benchmarked: B = 32 in one forward (x generated on the
     device from a seeded generator; 13 GB in, 13 GB out, 33 GB of workspace)."""

@@ -95,6 +95,31 @@ def test_streamed_fp64_oracle_matches_full_layer(B, S, d, H, causal):
     assert all(torch.isfinite(c).all() for c in ctx_rows_seen)
 
 
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_streamed_fp64_oracle_with_key_mask_matches_full_layer(causal):
+    """The streamed oracle with a key-padding mask (the long-context masked
+    check's oracle) equals the full reference layer given the same
+    valid_token_mask: padded keys get no probability (:106-109) and a padded
+    query row's attention output is zeroed (:121-122), sampled rows including
+    padded ones."""
+    B, S, d, H = 2, 333, 64, 2
+    cfg = TransformerConfig(B, S, d, H, causal=causal)
+    layer = build_reference_layer(cfg, 1234)
+    x, _ = generate_random_case(cfg, 1234)
+    g = torch.Generator().manual_seed(5)
+    mask = torch.stack([torch.arange(S) < 250,                       # padded tail
+                        torch.rand(S, generator=g) > 0.3])           # scattered
+    mask[1, 0] = True   # causal rows always see at least key 0
+    full = ReferenceLayer(d, H, causal).double()
+    full.load_state_dict(layer.state_dict())
+    with torch.inference_mode():
+        y_full = full(x.double(), mask)
+        for b in range(B):
+            rows = sample_rows(S, 41, seed=b)
+            y_rows = streamed_layer_rows_fp64(layer, x[b], rows, causal, key_mask=mask[b])
+            assert (y_rows - y_full[b, rows]).abs().max() <= 1e-5
+
+
 def test_fp32_oracle_within_gate_of_fp64():
     cfg = TransformerConfig(4, 128, 128, 4)
     layer = build_reference_layer(cfg, 1234)
