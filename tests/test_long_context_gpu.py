@@ -53,20 +53,22 @@ def test_cfg5_sampled_rows_fp64(pkg, cuda_ok, causal):
         assert rel < 1e-2, f"sequence {b}: ctx max error {rel:.3e} of max |ctx|"
 
 
-def test_cfg5_key_mask_sampled_rows_fp64(pkg, cuda_ok):
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_cfg5_key_mask_sampled_rows_fp64(pkg, cuda_ok, causal):
     """cfg5 shape with a key-padding mask (the masked long-context kernel):
     sequence 0 padded after 61234 tokens, sequence 1 with 30 % of its tokens
     scattered invalid. Sampled rows, valid and padded, against the fp64
     streamed oracle given the same mask (padded keys get no probability,
     padded rows y = LN2(x))."""
     B, S, d, H = 2, 100000, 1024, 16
-    cfg = TransformerConfig(B, S, d, H)
+    cfg = TransformerConfig(B, S, d, H, causal=causal)
     ref = build_reference_layer(cfg, 1234)
-    lay = pkg.B200TransformerLayer(d, H, use_graphs=False).cuda().eval()
+    lay = pkg.B200TransformerLayer(d, H, causal, use_graphs=False).cuda().eval()
     lay.load_state_dict(ref.state_dict(), strict=True)
     x, _ = generate_random_case(cfg, seed=4321)
     g = torch.Generator().manual_seed(77)
     mask = torch.stack([torch.arange(S) < 61234, torch.rand(S, generator=g) > 0.3])
+    mask[:, 0] = True   # a causal row always sees key 0
     with torch.inference_mode():
         y = lay(x.cuda(), mask.cuda())
         torch.cuda.synchronize()
@@ -76,7 +78,7 @@ def test_cfg5_key_mask_sampled_rows_fp64(pkg, cuda_ok):
     for b in range(B):
         rows = torch.unique(torch.cat([sample_rows(S, 200, seed=2000 + b),
                                        torch.tensor([0, 61233, 61234, 61235, 99999])]))
-        y_ref = streamed_layer_rows_fp64(ref, x[b], rows, False, key_mask=mask[b])
+        y_ref = streamed_layer_rows_fp64(ref, x[b], rows, causal, key_mask=mask[b])
         res = compare_outputs(y_ref, y[b, rows])
         assert res.passed, f"sequence {b}: {res}"
 
