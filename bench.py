@@ -431,7 +431,11 @@ def main() -> int:
     stream = torch.cuda.current_stream(dev)
     fused = fused_eligible(cfg)
     k_ms, total_ms = {}, 0.0
-    launches_per_step = 1 if fused else 3 + (2 if d > 256 else 0)
+    # K1: row LN + GEMM for d > 256, else one kernel; K2: one; K3: one (the
+    # LayerNorm-2 epilogue, clustered for d = 256 * {2, 3, 4, 6, 8}) or the
+    # residual GEMM + row LayerNorm for other d > 256.
+    k3_launches = 1 if d <= 256 or (d % 256 == 0 and d // 256 in (2, 3, 4, 6, 8)) else 2
+    launches_per_step = 1 if fused else (2 if d > 256 else 1) + 1 + k3_launches
 
     with torch.inference_mode():
         if Bl > 0:
