@@ -309,11 +309,11 @@ int launch_gemm_tma_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const 
 // Clusters of NC CTAs for the LayerNorm-2 out-projection (d = 256 NC): the
 // persistent grid holds as many clusters as can be resident at once (looked
 // up once per device and kernel), at most one per M tile.
-template <int NC, int ST>
+template <int NC, int ST, int BN = 256>
 int launch_gemm_ln_cluster_t(const CUtensorMap& map_a, const CUtensorMap& map_b, const EpiArgs& ea, long long T,
                              int K, void* ws, cudaStream_t st) {
-  using Cfg = GemmLnClusterCfg<NC, ST>;
-  auto kern = gemm_ln_cluster_kernel<NC, ST>;
+  using Cfg = GemmLnClusterCfg<NC, ST, BN>;
+  auto kern = gemm_ln_cluster_kernel<NC, ST, BN>;
   const int smem = Cfg::SMEM;
   int rc = ensure_smem((const void*)kern, smem);
   if (rc) return rc;
@@ -495,6 +495,17 @@ int run_outproj(const b200l_layer_desc* desc, const Plan& p, const float* x, flo
   if (p.d <= 256) {
     const int bn = (p.d + 63) / 64 * 64;
     if ((rc = map_rows_k(&map_b, desc->wo, (unsigned long long)p.d, p.d, (unsigned)bn, "wo"))) return rc;
+    if (bn == p.d) {
+      // d a multiple of 64: the row fits one CTA's accumulator exactly; the
+      // LayerNorm-2 kernel with the residual and y moved by TMA (a cluster of
+      // one CTA, so no statistics exchange).
+      switch (bn) {
+        case 64: return launch_gemm_ln_cluster_t<1, 3, 64>(map_a, map_b, ea, p.T, p.d, ws, st);
+        case 128: return launch_gemm_ln_cluster_t<1, 3, 128>(map_a, map_b, ea, p.T, p.d, ws, st);
+        case 192: return launch_gemm_ln_cluster_t<1, 3, 192>(map_a, map_b, ea, p.T, p.d, ws, st);
+        default: return launch_gemm_ln_cluster_t<1, 3, 256>(map_a, map_b, ea, p.T, p.d, ws, st);
+      }
+    }
     switch (bn) {
       case 64: return launch_gemm_tma_t<64, 2, EPI_RESID_LN>(map_a, map_b, ea, p.T, p.d, p.d, ws, st);
       case 128: return launch_gemm_tma_t<128, 2, EPI_RESID_LN>(map_a, map_b, ea, p.T, p.d, p.d, ws, st);

@@ -712,9 +712,10 @@ __global__ void __launch_bounds__(192, 1)
 // CTA loads its own A tile, its 256 rows of Wo and its x columns.
 // Warps: 0 A / B producer, 1 MMA issuer + TMEM owner, 2-5 epilogue, 6 x producer.
 // ===========================================================================
-template <int NC, int ST>
+template <int NC, int ST, int BN_ = 256>
 struct GemmLnClusterCfg {
-  static constexpr int BN = 256;
+  static constexpr int BN = BN_;                        // columns per CTA (= d when NC = 1)
+  static constexpr int TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);   // two accumulators
   static constexpr int A_BYTES = 128 * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE = A_BYTES + B_BYTES;
@@ -730,13 +731,13 @@ struct GemmLnClusterCfg {
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-template <int NC, int ST>
+template <int NC, int ST, int BN_ = 256>
 __global__ void __launch_bounds__(224, 1)
     gemm_ln_cluster_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                            const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_y,
                            EpiArgs ea, long long T, int K, DevStatus* status) {
   pdl_wait_then_release();
-  using C = GemmLnClusterCfg<NC, ST>;
+  using C = GemmLnClusterCfg<NC, ST, BN_>;
   constexpr int BN = C::BN;
   constexpr int XS = C::XS;
   constexpr int NCH = BN / 32;   // 32-column chunks per tile
@@ -786,7 +787,7 @@ __global__ void __launch_bounds__(224, 1)
     tma_prefetch_desc(&map_y);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
   // Every CTA's barriers are initialised before any peer may arrive on them.
@@ -920,29 +921,32 @@ __global__ void __launch_bounds__(224, 1)
       const float dmean = s1 * (1.0f / (float)BN);
       const float mean_l = shift + dmean;
       const float m2 = fmaxf(s2 - s1 * dmean, 0.f);   // squared deviations about mean_l
-      // Exchange (mean, M2) of this row with every CTA of the cluster: store
-      // the pair into each CTA's slot, then arrive (cluster-scope release of
-      // that store) on each CTA's stats barrier, which expects one arrival
-      // per epilogue thread of every CTA. Every wait stays bounded.
-      const int slot = ti & 1;
-      const uint32_t my_entry = smem_u32(&stats[(slot * NC + (int)rank) * 128 + row]);
-      const uint32_t bar_local = smem_u32(&stats_full[slot]);
+      float mean = mean_l, M2 = m2;
+      if constexpr (NC > 1) {
+        // Exchange (mean, M2) of this row with every CTA of the cluster: store
+        // the pair into each CTA's slot, then arrive (cluster-scope release of
+        // that store) on each CTA's stats barrier, which expects one arrival
+        // per epilogue thread of every CTA. Every wait stays bounded.
+        const int slot = ti & 1;
+        const uint32_t my_entry = smem_u32(&stats[(slot * NC + (int)rank) * 128 + row]);
+        const uint32_t bar_local = smem_u32(&stats_full[slot]);
 #pragma unroll 1
-      for (int q = 0; q < NC; ++q) {
-        st_cluster_v2(mapa_shared(my_entry, (uint32_t)q), mean_l, m2);
-        mbar_arrive_cluster(mapa_shared(bar_local, (uint32_t)q));
-      }
-      if (!__all_sync(0xffffffffu, mbar_wait_cluster(&stats_full[slot], (uint32_t)(ti >> 1) & 1, wc))) break;
-      float mean = 0.f;
+        for (int q = 0; q < NC; ++q) {
+          st_cluster_v2(mapa_shared(my_entry, (uint32_t)q), mean_l, m2);
+          mbar_arrive_cluster(mapa_shared(bar_local, (uint32_t)q));
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait_cluster(&stats_full[slot], (uint32_t)(ti >> 1) & 1, wc))) break;
+        mean = 0.f;
 #pragma unroll
-      for (int q = 0; q < NC; ++q) mean += stats[(slot * NC + q) * 128 + row].x;
-      mean *= 1.0f / (float)NC;
-      float M2 = 0.f;
+        for (int q = 0; q < NC; ++q) mean += stats[(slot * NC + q) * 128 + row].x;
+        mean *= 1.0f / (float)NC;
+        M2 = 0.f;
 #pragma unroll
-      for (int q = 0; q < NC; ++q) {
-        const float2 e = stats[(slot * NC + q) * 128 + row];
-        const float dm = e.x - mean;
-        M2 += e.y + (float)BN * dm * dm;
+        for (int q = 0; q < NC; ++q) {
+          const float2 e = stats[(slot * NC + q) * 128 + row];
+          const float dm = e.x - mean;
+          M2 += e.y + (float)BN * dm * dm;
+        }
       }
       const float rstd = rsqrtf(M2 * inv_d + ea.eps);
       // pass 3: normalise this CTA's columns into the warp's staging buffers
@@ -984,7 +988,7 @@ __global__ void __launch_bounds__(224, 1)
   if (threadIdx.x == 0 && waitctl_aborted(wc)) record_error(status, kErrTimeout, kGemmTma, 10 + NC);
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   // No CTA leaves while a peer may still write into its shared memory.
   cluster_sync_all();
