@@ -346,6 +346,9 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
 // stored back to back (SBO = 8 * row_bytes), LBO unused (1). The tile base must
 // be aligned to the atom (1024 B / 512 B); K steps inside a row advance the
 // start address by 32 B (16 fp16 elements).
+// The same descriptor, with the instruction descriptor's B-major bit set,
+// describes an MN-major B operand whose N extent is one swizzle row (32 fp16
+// for SWIZZLE_64B): K rows of `row_bytes`, 8-row groups SBO apart.
 __device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t saddr, int row_bytes) {
   const uint64_t layout = (row_bytes == 128) ? 2ull : 4ull;  // SWIZZLE_128B : SWIZZLE_64B
   uint64_t d = 0;

@@ -20,8 +20,8 @@
 //              after the last head, the out-projection accumulator [128, 128 + d)
 // so the next sequence's first q|k|v projection can run during the LN2 epilogue.
 // Shared memory per slot: A = LN1(x) fp16 (kept for every head's projection),
-// C = ctx fp16 (A operand of the out-projection), k [128 x 32] and v^T [32 x 128]
-// fp16 of the current head. Weight tiles (q|k|v rows of one head, then Wo)
+// C = ctx fp16 (A operand of the out-projection), k and v [128 keys x 32] fp16
+// of the current head (v is the MN-major B operand of P v). Weight tiles (q|k|v rows of one head, then Wo)
 // stream from L2 through a 2-deep TMA ring shared by both slots.
 // Warps: 0 TMA producer, 1 / 2 MMA issuers of slot 0 / 1 (warp 1 owns TMEM;
 // separate issuers keep one slot from stalling the other), 4-7 slot-0 rows, 8-11
@@ -61,7 +61,7 @@ struct FusedCfg {
   static constexpr int WBUF = ((WQ_BYTES > WO_BYTES ? WQ_BYTES : WO_BYTES) + 1023) / 1024 * 1024;
   static constexpr int A_BYTES = KC * 128 * 128;     // 128 token rows
   static constexpr int K_BYTES = 128 * 64;           // 128 keys x 32 fp16, 64-byte swizzle
-  static constexpr int V_BYTES = 2 * 32 * 128;       // v^T: 32 x 128 keys, two 64-key atom columns
+  static constexpr int V_BYTES = 128 * 64;           // 128 keys x 32 fp16, 64-byte swizzle (like k)
   static constexpr int SLOT = 2 * A_BYTES + K_BYTES + V_BYTES;
   static constexpr int PARAM_BYTES = 3 * DM * 4;     // bo, ln2_w, ln2_b in shared memory
   static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + PARAM_BYTES + 1024;
@@ -246,9 +246,10 @@ __global__ void __launch_bounds__(512, 1)
             tc_fence_after();
 #pragma unroll
             for (int k = 0; k < 8; ++k)
-              umma_f16_ts(t_slot + 96, t_slot + 128 + k * 8,
-                          sdesc_kmajor(vbase + (uint32_t)(k >> 2) * 4096 + (k & 3) * 32, 128), id_o,
-                          k > 0 ? 1u : 0u);
+              // B = v [16 keys x 32] rows of 64 B from key 16k: MN-major, one
+              // 32-column swizzle atom along N, 8-key row groups 512 B apart.
+              umma_f16_ts(t_slot + 96, t_slot + 128 + k * 8, sdesc_kmajor(vbase + (uint32_t)k * 1024, 64),
+                          id_o | (1u << 16), k > 0 ? 1u : 0u);
             umma_commit(sb(s, FB_O_FULL));
           }
         }
@@ -417,7 +418,7 @@ __global__ void __launch_bounds__(512, 1)
       bool ok = true;
       for (int h = 0; h < H; ++h) {
         const int n = pi * H + h;
-        // ---- q|k|v of head h: bias, fp16; q -> TMEM, k and v^T -> shared memory
+        // ---- q|k|v of head h: bias, fp16; q -> TMEM, k and v -> shared memory
         if (!mbar_wait_warp(sb(s, FB_QKV_FULL), n & 1, wc)) { ok = false; break; }
         tc_fence_after();
         {
@@ -452,9 +453,9 @@ __global__ void __launch_bounds__(512, 1)
             st_shared_v4(k_base + row * 64 + ((c ^ ((row >> 1) & 3)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
                          pk[4 * c + 3]);
           tmem_ld32(tb + 64, r);
+          // v row of this token, laid out like k ([128 keys x 32] fp16,
+          // 64-byte swizzle): the P v MMAs read it as an MN-major B operand.
           const float4* bv = reinterpret_cast<const float4*>(a.bqkv + 2 * DM + 32 * h);
-          const uint32_t vrow = v_base + (uint32_t)(row >> 6) * 4096 + (row & 7) * 2;
-          const int vch = (row & 63) >> 3;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float4 bb = __ldg(bv + i);
@@ -462,13 +463,13 @@ __global__ void __launch_bounds__(512, 1)
                                           make_float2(bb.x, bb.y));
             const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
                                           make_float2(bb.z, bb.w));
-            const float vv[4] = {v01.x, v01.y, v23.x, v23.y};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int j = 4 * i + e;
-              st_shared_u16(vrow + j * 128 + ((vch ^ (j & 7)) << 4), __half_as_ushort(__float2half_rn(vv[e])));
-            }
+            pk[2 * i] = pack_half2(v01.x, v01.y);
+            pk[2 * i + 1] = pack_half2(v23.x, v23.y);
           }
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            st_shared_v4(v_base + row * 64 + ((c ^ ((row >> 1) & 3)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                         pk[4 * c + 3]);
         }
         fence_proxy_async_smem();
         tc_fence_before();
