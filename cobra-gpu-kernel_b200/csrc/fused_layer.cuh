@@ -13,16 +13,22 @@
 // Two sequences are processed in lockstep, one per worker warpgroup, so the
 // tensor core alternates between them while the other one is in its
 // LayerNorm / softmax / epilogue. Per sequence slot, TMEM (256 columns):
-//   [0, 96)    q|k|v projection of one head (fp32)
-//   [96, 112)  q of the head as fp16 pairs (A operand of S = q k^T, read from TMEM)
+//   [0, 96)    q|k|v projection of one head (fp32); once read, q of the head
+//              as fp16 pairs in [0, 16) (A operand of S = q k^T, from TMEM)
 //   [96, 128)  O = P v of the head (fp32)
 //   [128, 256) S = q k^T (fp32); P (fp16 pairs) overwrites [128, 192) in place;
 //              after the last head, the out-projection accumulator [128, 128 + d)
 // so the next sequence's first q|k|v projection can run during the LN2 epilogue.
 // Shared memory per slot: A = LN1(x) fp16 (kept for every head's projection),
-// C = ctx fp16 (A operand of the out-projection), k and v [128 keys x 32] fp16
-// of the current head (v is the MN-major B operand of P v). Weight tiles (q|k|v rows of one head, then Wo)
-// stream from L2 through a 2-deep TMA ring shared by both slots.
+// C = ctx fp16 (A operand of the out-projection) as one [128 x 32] block of
+// 64-byte rows per head, k [128 keys x 32] fp16 of the current head. v of
+// head h is stored in ctx block h (token rows, 64-byte swizzle, the MN-major B
+// operand of P v) and ctx of head h overwrites it once that P v completed.
+// Weight tiles (q|k|v rows of one head, then Wo) stream from L2 through a
+// 2-deep TMA ring shared by both slots.
+// Per head the row warps run softmax(h), then the q|k|v epilogue of head h+1
+// while P v of head h runs, then ctx(h): the P v and next-S round trips of the
+// tensor core overlap row work instead of stalling it.
 // Warps: 0 TMA producer, 1 / 2 MMA issuers of slot 0 / 1 (warp 1 owns TMEM;
 // separate issuers keep one slot from stalling the other), 4-7 slot-0 rows, 8-11
 // slot-1 rows (one token row per thread: q|k|v epilogue, softmax, ctx, LN2),
@@ -60,9 +66,10 @@ struct FusedCfg {
   static constexpr int WO_BYTES = KC * DM * 128;     // Wo
   static constexpr int WBUF = ((WQ_BYTES > WO_BYTES ? WQ_BYTES : WO_BYTES) + 1023) / 1024 * 1024;
   static constexpr int A_BYTES = KC * 128 * 128;     // 128 token rows
-  static constexpr int K_BYTES = 128 * 64;           // 128 keys x 32 fp16, 64-byte swizzle
-  static constexpr int V_BYTES = 128 * 64;           // 128 keys x 32 fp16, 64-byte swizzle (like k)
-  static constexpr int SLOT = 2 * A_BYTES + K_BYTES + V_BYTES;
+  // k of the current head (128 keys x 32 fp16, 64-byte swizzle, 8 KB); the
+  // buffer holds one 32-column fp32 chunk of x / y in the LN2 epilogue.
+  static constexpr int KX_BYTES = 16384;
+  static constexpr int SLOT = 2 * A_BYTES + KX_BYTES;
   static constexpr int PARAM_BYTES = 3 * DM * 4;     // bo, ln2_w, ln2_b in shared memory
   static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + PARAM_BYTES + 1024;
   static_assert(SMEM <= 232448, "fits the 227 KB opt-in shared memory of one CTA");
@@ -70,7 +77,6 @@ struct FusedCfg {
   // d = 128: the fourth 32-column chunk of x and y is staged in the weight
   // buffer that held Wo, once both slots' out-projections have read it.
   static constexpr bool WO_STAGE = DM / 32 > 3;
-  static_assert(K_BYTES + V_BYTES == 16384, "k|v buffer holds one 32-column fp32 chunk of x");
 };
 
 enum FusedBar : int { FB_A_READY = 0, FB_A_FREE, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY,
@@ -101,7 +107,6 @@ __global__ void __launch_bounds__(512, 1)
   auto slot_a = [&](int s) { return sSlot + s * C::SLOT; };
   auto slot_c = [&](int s) { return sSlot + s * C::SLOT + C::A_BYTES; };
   auto slot_k = [&](int s) { return sSlot + s * C::SLOT + 2 * C::A_BYTES; };
-  auto slot_v = [&](int s) { return sSlot + s * C::SLOT + 2 * C::A_BYTES + C::K_BYTES; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npairs = (a.B + 1) / 2;
@@ -128,8 +133,8 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(sb(s, FB_X2), 1);
       mbar_init(sb(s, FB_X3), 1);
       mbar_init(sb(s, FB_Y_STAGED), 4);   // every row warp has written its y rows
-      mbar_init(sb(s, FB_Y_READ), 1);     // the leader saw TMA finish reading the k|v chunk
-      mbar_init(sb(s, FB_Y_CTX), 1);      // ... and the ctx chunks
+      mbar_init(sb(s, FB_Y_READ), 1);     // the leader saw TMA finish reading y chunks 0-1 (and 3)
+      mbar_init(sb(s, FB_Y_CTX), 1);      // ... and y chunk 2
     }
     mbar_init(mma_done, 2);
     mbar_init(wo_done, 2);
@@ -194,7 +199,6 @@ __global__ void __launch_bounds__(512, 1)
       const uint32_t abase = smem_u32(slot_a(s));
       const uint32_t cbase = smem_u32(slot_c(s));
       const uint32_t kbase = smem_u32(slot_k(s));
-      const uint32_t vbase = smem_u32(slot_v(s));
       int wt = 0, pi = 0;
       bool ok = true;
       // q|k|v projection of head h from weight tile wt; both slots' issuers
@@ -230,27 +234,35 @@ __global__ void __launch_bounds__(512, 1)
         if (!issue_qkv(0, active)) { ok = false; break; }
         for (int h = 0; h < H && ok; ++h) {
           const int n = pi * H + h;
-          if (active) {  // S = q k^T, q from TMEM
+          if (active) {  // S = q k^T, q (fp16) from TMEM [0, 16)
+            // S overwrites P of the previous head: its P v completed (waited below).
             if (!mbar_wait(sb(s, FB_KQV_READY), n & 1, wc)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int k = 0; k < 2; ++k)
-              umma_f16_ts(t_slot + 128, t_slot + 96 + k * 8, sdesc_kmajor(kbase + k * 32, 64), id_s,
-                          k > 0 ? 1u : 0u);
+              umma_f16_ts(t_slot + 128, t_slot + k * 8, sdesc_kmajor(kbase + k * 32, 64), id_s, k > 0 ? 1u : 0u);
             umma_commit(sb(s, FB_S_FULL));
           }
-          // next head's projection runs while this head's softmax does
-          if (h + 1 < H && !issue_qkv(h + 1, active)) { ok = false; break; }
+          // The next head's projection runs while this head's softmax does; it
+          // overwrites q in [0, 16), so it waits for this S to complete.
+          if (h + 1 < H) {
+            if (active && !mbar_wait(sb(s, FB_S_FULL), n & 1, wc)) { ok = false; break; }
+            if (!issue_qkv(h + 1, active)) { ok = false; break; }
+          }
           if (active) {  // O = P v, P from TMEM
             if (!mbar_wait(sb(s, FB_P_READY), n & 1, wc)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int k = 0; k < 8; ++k)
-              // B = v [16 keys x 32] rows of 64 B from key 16k: MN-major, one
-              // 32-column swizzle atom along N, 8-key row groups 512 B apart.
-              umma_f16_ts(t_slot + 96, t_slot + 128 + k * 8, sdesc_kmajor(vbase + (uint32_t)k * 1024, 64),
-                          id_o | (1u << 16), k > 0 ? 1u : 0u);
+              // B = v [16 keys x 32] in ctx block h, rows of 64 B from key 16k:
+              // MN-major, one 32-column swizzle atom along N, 8-key row groups
+              // 512 B apart.
+              umma_f16_ts(t_slot + 96, t_slot + 128 + k * 8,
+                          sdesc_kmajor(cbase + (uint32_t)h * 8192 + (uint32_t)k * 1024, 64), id_o | (1u << 16),
+                          k > 0 ? 1u : 0u);
             umma_commit(sb(s, FB_O_FULL));
+            // The next S (or the out-projection) overwrites P: wait for this P v.
+            if (!mbar_wait(sb(s, FB_O_FULL), n & 1, wc)) { ok = false; break; }
           }
         }
         if (!ok) break;
@@ -263,9 +275,10 @@ __global__ void __launch_bounds__(512, 1)
             const uint32_t wbase = smem_u32(sW + b * C::WBUF);
 #pragma unroll
             for (int k = 0; k < DM / 16; ++k) {
-              const uint32_t oc = (uint32_t)(k >> 2) * 16384 + (k & 3) * 32;
+              // ctx: one [128 x 32] fp16 block per head, 64-byte rows
+              const uint32_t oc = (uint32_t)(k >> 1) * 8192 + (k & 1) * 32;
               const uint32_t ow = (uint32_t)(k >> 2) * (DM * 128) + (k & 3) * 32;
-              umma_f16_ss(t_slot + 128, sdesc_kmajor(cbase + oc, 128), sdesc_kmajor(wbase + ow, 128), id_out,
+              umma_f16_ss(t_slot + 128, sdesc_kmajor(cbase + oc, 64), sdesc_kmajor(wbase + ow, 128), id_out,
                           k > 0 ? 1u : 0u);
             }
             umma_commit(sb(s, FB_OUT_FULL));
@@ -378,20 +391,30 @@ __global__ void __launch_bounds__(512, 1)
     const uint32_t tb = tmem_base + (uint32_t)(s * 256) + ((uint32_t)(q * 32) << 16);
     const uint32_t c_base = smem_u32(slot_c(s));
     const uint32_t k_base = smem_u32(slot_k(s));
-    const uint32_t v_base = smem_u32(slot_v(s));
     const float sl2 = a.scale_log2;
     const float inv_d = 1.0f / (float)DM;
     int pi = 0;
+    constexpr int NXC = DM / 32;   // 32-column fp32 chunks of x / y per row: 4 (d=128) or 2 (d=64)
+    const bool leader = (q == 0 && lane == 0);
     for (int pair = blockIdx.x; pair < npairs; pair += gridDim.x, ++pi) {
       const int seq = 2 * pair + s;
+      // The previous sequence's y stores, bulk groups in issue order: [chunk 3
+      // (weight buffer)], [chunks 0-1 (k buffer, ctx blocks 0-1)], [chunk 2
+      // (ctx blocks 2-3)]. Once the first two have read shared memory, the
+      // weight buffer goes back to the ring (also when this slot has no
+      // sequence left) and this sequence may write k, v(0) and v(1).
+      if (pi > 0 && leader) {
+        if constexpr (C::WO_STAGE) {
+          bulk_wait_read<1>();
+          mbar_arrive(&w_empty[((pi - 1) * (H + 1) + H) & 1]);
+        } else {
+          bulk_wait_read_all();
+        }
+      }
       if (seq >= a.B) break;
       const long long t0 = (long long)seq * S;
-      const bool leader = (q == 0 && lane == 0);
-      if (pi > 0) {   // the previous sequence's y store out of k|v must have read it
-        if (leader) {
-          bulk_wait_read<1>();   // groups: ([chunk 3]), [chunk 0: k|v], [chunks 1-2: ctx]
-          mbar_arrive(sb(s, FB_Y_READ));
-        }
+      if (pi > 0) {
+        if (leader) mbar_arrive(sb(s, FB_Y_READ));
         if (!mbar_wait_warp(sb(s, FB_Y_READ), (pi - 1) & 1, wc)) break;
       }
       // Keys this row may see, one bit each: valid (mask), inside S, causal.
@@ -415,62 +438,55 @@ __global__ void __launch_bounds__(512, 1)
         }
       }
       const bool full = KMASK ? (vb[0] & vb[1] & vb[2] & vb[3]) == 0xffffffffu : (lim == 128);
-      bool ok = true;
-      for (int h = 0; h < H; ++h) {
+      // q|k|v epilogue of head h: bias, fp16; q -> TMEM [0, 16) (the A operand
+      // of S), k -> the k buffer, v -> ctx block h (read by P v of head h
+      // before ctx of head h is written there).
+      auto qkv_epilogue = [&](int h) -> bool {
         const int n = pi * H + h;
-        // ---- q|k|v of head h: bias, fp16; q -> TMEM, k and v -> shared memory
-        if (!mbar_wait_warp(sb(s, FB_QKV_FULL), n & 1, wc)) { ok = false; break; }
-        tc_fence_after();
-        {
-          uint32_t r[32], pk[16];
-          tmem_ld32(tb + 0, r);
-          const float4* bq = reinterpret_cast<const float4*>(a.bqkv + 32 * h);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 bb = __ldg(bq + i);
-            const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
-                                          make_float2(bb.x, bb.y));
-            const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
-                                          make_float2(bb.z, bb.w));
-            pk[2 * i] = pack_half2(v01.x, v01.y);
-            pk[2 * i + 1] = pack_half2(v23.x, v23.y);
+        if (NXC > 2 && h == 2 && pi > 0) {   // ctx blocks 2-3: the y chunk-2 store has read them
+          if (leader) {
+            bulk_wait_read_all();
+            mbar_arrive(sb(s, FB_Y_CTX));
           }
-          tmem_st16(tb + 96, pk);
-          tmem_ld32(tb + 32, r);
-          const float4* bk = reinterpret_cast<const float4*>(a.bqkv + DM + 32 * h);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 bb = __ldg(bk + i);
-            const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
-                                          make_float2(bb.x, bb.y));
-            const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
-                                          make_float2(bb.z, bb.w));
-            pk[2 * i] = pack_half2(v01.x, v01.y);
-            pk[2 * i + 1] = pack_half2(v23.x, v23.y);
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            st_shared_v4(k_base + row * 64 + ((c ^ ((row >> 1) & 3)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
-                         pk[4 * c + 3]);
-          tmem_ld32(tb + 64, r);
-          // v row of this token, laid out like k ([128 keys x 32] fp16,
-          // 64-byte swizzle): the P v MMAs read it as an MN-major B operand.
-          const float4* bv = reinterpret_cast<const float4*>(a.bqkv + 2 * DM + 32 * h);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 bb = __ldg(bv + i);
-            const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
-                                          make_float2(bb.x, bb.y));
-            const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
-                                          make_float2(bb.z, bb.w));
-            pk[2 * i] = pack_half2(v01.x, v01.y);
-            pk[2 * i + 1] = pack_half2(v23.x, v23.y);
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            st_shared_v4(v_base + row * 64 + ((c ^ ((row >> 1) & 3)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
-                         pk[4 * c + 3]);
+          if (!mbar_wait_warp(sb(s, FB_Y_CTX), (pi - 1) & 1, wc)) return false;
         }
+        if (!mbar_wait_warp(sb(s, FB_QKV_FULL), n & 1, wc)) return false;
+        tc_fence_after();
+        uint32_t r[32], pk[16];
+        tmem_ld32(tb + 0, r);
+        const float4* bq = reinterpret_cast<const float4*>(a.bqkv + 32 * h);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 bb = __ldg(bq + i);
+          const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                        make_float2(bb.x, bb.y));
+          const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                        make_float2(bb.z, bb.w));
+          pk[2 * i] = pack_half2(v01.x, v01.y);
+          pk[2 * i + 1] = pack_half2(v23.x, v23.y);
+        }
+        tmem_st16(tb + 0, pk);
+        // k, then v: token rows of 64 bytes, 64-byte swizzle
+        auto kv_row = [&](int part, uint32_t dst) {
+          tmem_ld32(tb + 32 * part, r);
+          const float4* bb4 = reinterpret_cast<const float4*>(a.bqkv + part * DM + 32 * h);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(bb4 + i);
+            const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                          make_float2(bb.x, bb.y));
+            const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                          make_float2(bb.z, bb.w));
+            pk[2 * i] = pack_half2(v01.x, v01.y);
+            pk[2 * i + 1] = pack_half2(v23.x, v23.y);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            st_shared_v4(dst + row * 64 + ((c ^ ((row >> 1) & 3)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                         pk[4 * c + 3]);
+        };
+        kv_row(1, k_base);
+        kv_row(2, c_base + (uint32_t)h * 8192);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
@@ -478,6 +494,11 @@ __global__ void __launch_bounds__(512, 1)
           mbar_arrive(sb(s, FB_QKV_FREE));   // q|k|v accumulator [0, 96) read
           mbar_arrive(sb(s, FB_KQV_READY));
         }
+        return true;
+      };
+      bool ok = qkv_epilogue(0);
+      for (int h = 0; h < H && ok; ++h) {
+        const int n = pi * H + h;
         // ---- softmax of S = q k^T (one row per thread, exact: S <= 128 keys)
         if (!mbar_wait_warp(sb(s, FB_S_FULL), n & 1, wc)) { ok = false; break; }
         tc_fence_after();
@@ -530,27 +551,20 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_P_READY));
-        // ---- ctx columns of head h = O / l, fp16, into the out-projection operand
+        // ---- the next head's q|k|v epilogue while this head's P v runs
+        if (h + 1 < H && !qkv_epilogue(h + 1)) { ok = false; break; }
+        // ---- ctx columns of head h = O / l, fp16, into ctx block h (over v of head h)
         if (!mbar_wait_warp(sb(s, FB_O_FULL), n & 1, wc)) { ok = false; break; }
         tc_fence_after();
-        if (h == 0 && pi > 0) {   // the previous sequence's y stores out of ctx have read it
-          if (leader) {
-            bulk_wait_read_all();
-            mbar_arrive(sb(s, FB_Y_CTX));
-          }
-          if (!mbar_wait_warp(sb(s, FB_Y_CTX), (pi - 1) & 1, wc)) { ok = false; break; }
-        }
         {
           uint32_t r[32];
           tmem_ld32(tb + 96, r);
           const float il = l > 0.f ? 1.0f / l : 0.f;
           const float2 il2 = make_float2(il, il);
-          const int col0 = 32 * h;
-          const uint32_t cb = c_base + (uint32_t)(col0 >> 6) * 16384 + row * 128;
-          const int ch0 = (col0 & 63) >> 3;
+          const uint32_t cb = c_base + (uint32_t)h * 8192 + row * 64;
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            st_shared_v4(cb + (((ch0 + c) ^ (row & 7)) << 4),
+            st_shared_v4(cb + ((c ^ ((row >> 1) & 3)) << 4),
                          pack_f2h(__fmul2_rn(make_float2(__uint_as_float(r[8 * c + 0]), __uint_as_float(r[8 * c + 1])), il2)),
                          pack_f2h(__fmul2_rn(make_float2(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3])), il2)),
                          pack_f2h(__fmul2_rn(make_float2(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5])), il2)),
@@ -569,7 +583,6 @@ __global__ void __launch_bounds__(512, 1)
       // read it, chunk 3 (d = 128) into this slot's half of the weight buffer
       // that held Wo, once both slots' out-projections have read it. y leaves
       // through the same four buffers.
-      constexpr int NXC = DM / 32;                       // 4 (d=128) or 2 (d=64)
       // Chunks per TMEM round trip in the LN2 passes: two (64 columns) where
       // registers allow; the masked variant keeps one.
       constexpr int CPR = KMASK ? 1 : 2;
@@ -700,24 +713,23 @@ __global__ void __launch_bounds__(512, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(sb(s, FB_Y_STAGED));
         if (leader && mbar_wait(sb(s, FB_Y_STAGED), pi & 1, wc)) {
-          // Three bulk groups, in the order their buffers are needed again:
-          // chunk 3 (the weight buffer), chunk 0 (k|v, the next sequence's
-          // first epilogue), chunks 1-2 (ctx, after its first softmax).
+          // Bulk groups in the order their buffers are needed again: chunk 3
+          // (the weight buffer, back to the ring), chunks 0-1 (the k buffer
+          // and ctx blocks 0-1: k, v(0), v(1) of the next sequence), chunk 2
+          // (ctx blocks 2-3: v(2), v(3)). The leader waits for them at the
+          // start of the next sequence and before its v(2).
           if constexpr (C::WO_STAGE) {
             tma_store_3d_hint(&map_y, wbuf, 96, 0, seq, pol_once);
             bulk_commit();
           }
           tma_store_3d_hint(&map_y, xchunk(0), 0, 0, seq, pol_once);
+          tma_store_3d_hint(&map_y, xchunk(1), 32, 0, seq, pol_once);
           bulk_commit();
-          for (int cc = 1; cc < NXC && cc < 3; ++cc) tma_store_3d_hint(&map_y, xchunk(cc), cc * 32, 0, seq, pol_once);
-          bulk_commit();
-          if constexpr (C::WO_STAGE) {
-            bulk_wait_read<2>();
-            mbar_arrive(&w_empty[wo_b]);
+          if constexpr (NXC > 2) {
+            tma_store_3d_hint(&map_y, xchunk(2), 64, 0, seq, pol_once);
+            bulk_commit();
           }
         }
-        // k|v and ctx are rewritten by the next sequence: the leader waits for
-        // TMA to have read them just before (start of the sequence / first ctx).
       }
       tc_fence_before();   // TMEM reads of this sequence done before the next S MMA
     }
