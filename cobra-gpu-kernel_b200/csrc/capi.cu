@@ -536,13 +536,13 @@ int launch_fused_t(const b200l_layer_desc* desc, const Plan& p, const DevInfo& d
   int rc = map_rows_k(&map_wqkv, desc->wqkv, 3ull * DM, DM, 32, "wqkv");
   if (rc) return rc;
   if ((rc = map_rows_k(&map_wo, desc->wo, (unsigned long long)DM, DM, DM, "wo"))) return rc;
-  // x and y viewed as [B][S][d] fp32 in 128-row x 32-column boxes: rows past S
-  // read as zero and are clipped on store.
+  // x and y viewed as [B][S][d] fp32 in 32-row x 32-column boxes (one row
+  // warp's rows of one chunk): rows past S read as zero and are clipped on store.
   CUtensorMap map_x, map_y;
   {
     const unsigned long long dims[3] = {(unsigned long long)DM, (unsigned long long)p.S, (unsigned long long)p.B};
     const unsigned long long strides[2] = {(unsigned long long)DM * 4, (unsigned long long)p.S * DM * 4};
-    const unsigned box[3] = {32, 128, 1};
+    const unsigned box[3] = {32, 32, 1};
     if ((rc = make_map(&map_x, x, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "x",
                        CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
       return rc;

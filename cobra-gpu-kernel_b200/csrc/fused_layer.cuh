@@ -34,9 +34,14 @@
 // slot-1 rows (one token row per thread: q|k|v epilogue, softmax, ctx, LN2),
 // 12-15 LayerNorm-1 of each slot's next sequence (warp per row, 16 rows of
 // loads in flight), so x loads stay off the critical path. In the LN2
-// epilogue the residual x arrives by TMA in 32-column chunks through the free
-// k|v buffer and y leaves by TMA stores, so both move as full 128-byte lines.
+// epilogue each row warp loads its rows of the residual x and stores its rows
+// of y by TMA (32-row x 32-column boxes through the k buffer and the ctx
+// halves), so both move as full 128-byte lines; the warps of a slot meet only
+// at the start of the next sequence (its k, v and ctx rows overlap other
+// warps' x / y rows), and nothing ties the two slots together there.
 #pragma once
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -73,15 +78,13 @@ struct FusedCfg {
   static constexpr int PARAM_BYTES = 3 * DM * 4;     // bo, ln2_w, ln2_b in shared memory
   static constexpr int SMEM = 2 * WBUF + 2 * SLOT + 512 + PARAM_BYTES + 1024;
   static_assert(SMEM <= 232448, "fits the 227 KB opt-in shared memory of one CTA");
-  static_assert(4 + 2 * 17 + 4 <= 64, "barrier block fits in 512 bytes");
-  // d = 128: the fourth 32-column chunk of x and y is staged in the weight
-  // buffer that held Wo, once both slots' out-projections have read it.
-  static constexpr bool WO_STAGE = DM / 32 > 3;
+  static_assert(4 + 2 * 23 + 6 <= 64, "barrier block fits in 512 bytes");
 };
 
+// Per sequence slot; FB_XW + 3 q + i: row warp q's x chunk 0 (i = 0),
+// chunks 1-2 (1) and chunk 3 (2).
 enum FusedBar : int { FB_A_READY = 0, FB_A_FREE, FB_QKV_FULL, FB_QKV_FREE, FB_KQV_READY, FB_S_FULL, FB_P_READY,
-                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_X0, FB_X1, FB_X2, FB_X3,
-                      FB_Y_STAGED, FB_Y_READ, FB_Y_CTX, FB_COUNT };
+                      FB_O_FULL, FB_CTX_READY, FB_OUT_FULL, FB_Y_READ, FB_XW, FB_COUNT = FB_XW + 12 };
 
 template <int DM, bool KMASK>   // KMASK: a key-padding mask may be given
 __global__ void __launch_bounds__(512, 1)
@@ -100,7 +103,6 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* mma_done = bars + 4 + 2 * FB_COUNT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   WaitCtl* wc = reinterpret_cast<WaitCtl*>(mma_done + 4);   // slots 4-5 past mma_done
-  uint64_t* wo_done = mma_done + 3;   // both slots' out-projections have read Wo
   // bo | ln2_w | ln2_b, read by every row thread in the out-projection epilogue.
   float* sprm = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);
   auto sb = [&](int s, int i) { return bars + 4 + FB_COUNT * s + i; };
@@ -128,16 +130,10 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(sb(s, FB_O_FULL), 1);
       mbar_init(sb(s, FB_CTX_READY), 4);
       mbar_init(sb(s, FB_OUT_FULL), 1);
-      mbar_init(sb(s, FB_X0), 1);
-      mbar_init(sb(s, FB_X1), 1);
-      mbar_init(sb(s, FB_X2), 1);
-      mbar_init(sb(s, FB_X3), 1);
-      mbar_init(sb(s, FB_Y_STAGED), 4);   // every row warp has written its y rows
-      mbar_init(sb(s, FB_Y_READ), 1);     // the leader saw TMA finish reading y chunks 0-1 (and 3)
-      mbar_init(sb(s, FB_Y_CTX), 1);      // ... and y chunk 2
+      mbar_init(sb(s, FB_Y_READ), 4);     // every row warp's y stores have read the chunk buffers
+      for (int i = 0; i < 12; ++i) mbar_init(sb(s, FB_XW + i), 1);
     }
     mbar_init(mma_done, 2);
-    mbar_init(wo_done, 2);
     waitctl_init(wc, status);
     fence_barrier_init();
     tma_prefetch_desc(&map_wqkv);
@@ -283,10 +279,7 @@ __global__ void __launch_bounds__(512, 1)
             }
             umma_commit(sb(s, FB_OUT_FULL));
           }
-          // With WO_STAGE the row leaders release this buffer after staging
-          // x / y chunk 3 in it.
-          if constexpr (C::WO_STAGE) umma_commit(wo_done);
-          else umma_commit(&w_empty[b]);
+          umma_commit(&w_empty[b]);
           ++wt;
         }
       }
@@ -395,26 +388,18 @@ __global__ void __launch_bounds__(512, 1)
     const float inv_d = 1.0f / (float)DM;
     int pi = 0;
     constexpr int NXC = DM / 32;   // 32-column fp32 chunks of x / y per row: 4 (d=128) or 2 (d=64)
-    const bool leader = (q == 0 && lane == 0);
     for (int pair = blockIdx.x; pair < npairs; pair += gridDim.x, ++pi) {
       const int seq = 2 * pair + s;
-      // The previous sequence's y stores, bulk groups in issue order: [chunk 3
-      // (weight buffer)], [chunks 0-1 (k buffer, ctx blocks 0-1)], [chunk 2
-      // (ctx blocks 2-3)]. Once the first two have read shared memory, the
-      // weight buffer goes back to the ring (also when this slot has no
-      // sequence left) and this sequence may write k, v(0) and v(1).
-      if (pi > 0 && leader) {
-        if constexpr (C::WO_STAGE) {
-          bulk_wait_read<1>();
-          mbar_arrive(&w_empty[((pi - 1) * (H + 1) + H) & 1]);
-        } else {
-          bulk_wait_read_all();
-        }
-      }
       if (seq >= a.B) break;
       const long long t0 = (long long)seq * S;
+      // k, v and ctx rows (64 bytes) overlap other warps' rows of the x / y
+      // chunks (128 bytes): every row warp's y stores of the previous
+      // sequence must have read the buffers before this sequence writes them.
       if (pi > 0) {
-        if (leader) mbar_arrive(sb(s, FB_Y_READ));
+        if (lane == 0) {
+          bulk_wait_read_all();
+          mbar_arrive(sb(s, FB_Y_READ));
+        }
         if (!mbar_wait_warp(sb(s, FB_Y_READ), (pi - 1) & 1, wc)) break;
       }
       // Keys this row may see, one bit each: valid (mask), inside S, causal.
@@ -443,13 +428,6 @@ __global__ void __launch_bounds__(512, 1)
       // before ctx of head h is written there).
       auto qkv_epilogue = [&](int h) -> bool {
         const int n = pi * H + h;
-        if (NXC > 2 && h == 2 && pi > 0) {   // ctx blocks 2-3: the y chunk-2 store has read them
-          if (leader) {
-            bulk_wait_read_all();
-            mbar_arrive(sb(s, FB_Y_CTX));
-          }
-          if (!mbar_wait_warp(sb(s, FB_Y_CTX), (pi - 1) & 1, wc)) return false;
-        }
         if (!mbar_wait_warp(sb(s, FB_QKV_FULL), n & 1, wc)) return false;
         tc_fence_after();
         uint32_t r[32], pk[16];
@@ -577,48 +555,31 @@ __global__ void __launch_bounds__(512, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(sb(s, FB_CTX_READY));
       // ---- out-projection epilogue: r = x + (acc + bo), LN2, y.
-      // The residual x arrives by TMA as 128-row x 32-column fp32 chunks (16 KB,
-      // 128-byte swizzle): chunk 0 into the k|v buffer (free since the last
-      // P v), chunks 1-2 into the two halves of ctx once the out-projection has
-      // read it, chunk 3 (d = 128) into this slot's half of the weight buffer
-      // that held Wo, once both slots' out-projections have read it. y leaves
-      // through the same four buffers.
-      // Chunks per TMEM round trip in the LN2 passes: two (64 columns) where
-      // registers allow; the masked variant keeps one.
-      constexpr int CPR = KMASK ? 1 : 2;
-      auto tmem_ld_cols = [&](uint32_t taddr, uint32_t (&rr)[32 * CPR]) {
-        if constexpr (CPR == 2) tmem_ld64(taddr, rr);
-        else tmem_ld32(taddr, rr);
+      // Each row warp moves its own 32 rows: lane 0 loads x and stores y as
+      // 32-row x 32-column fp32 TMA boxes (4 KB, 128-byte swizzle) through
+      // three 16 KB chunk buffers of the slot -- chunk 0, then chunk 3, through
+      // the k buffer (free since the last S), chunks 1-2 through the two halves
+      // of ctx once the out-projection has read it. Within the epilogue every
+      // buffer is used row by row, so no barrier couples the warps here, nor
+      // the two slots.
+      uint8_t* kxp = slot_k(s);
+      uint8_t* cxp = slot_c(s);
+      auto xchunk = [&](int cc) -> uint8_t* { return (cc == 0 || cc == 3) ? kxp : cxp + (cc - 1) * 16384; };
+      uint64_t* xbar = sb(s, FB_XW + 3 * q);   // this warp's x chunk 0 | chunks 1-2 | chunk 3
+      auto x_load = [&](int cc, uint64_t* bar) {
+        tma_load_3d_hint(xchunk(cc) + q * 4096, &map_x, bar, cc * 32, q * 32, seq, pol_once);
       };
-      auto tmem_st_cols = [&](uint32_t taddr, uint32_t (&rr)[32 * CPR]) {
-        if constexpr (CPR == 2) tmem_st64(taddr, rr);
-        else tmem_st32(taddr, rr);
-      };
-      uint8_t* xbuf = slot_k(s);
-      uint8_t* cbuf = slot_c(s);
-      const int wo_b = (pi * (H + 1) + H) & 1;           // ring buffer of this pair's Wo tile
-      uint8_t* wbuf = sW + wo_b * C::WBUF + s * 16384;
-      auto xchunk = [&](int cc) -> uint8_t* {
-        return cc == 0 ? xbuf : (cc == 3 ? wbuf : cbuf + (cc - 1) * 16384);
-      };
-      if (leader) {
-        mbar_arrive_expect_tx(sb(s, FB_X0), 16384);
-        tma_load_3d_hint(xbuf, &map_x, sb(s, FB_X0), 0, 0, seq, pol_once);
+      auto y_store = [&](int cc) { tma_store_3d_hint(&map_y, xchunk(cc) + q * 4096, cc * 32, q * 32, seq, pol_once); };
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&xbar[0], 4096);
+        x_load(0, &xbar[0]);
       }
       if (!mbar_wait_warp(sb(s, FB_OUT_FULL), pi & 1, wc)) break;
       tc_fence_after();
-      if (leader) {
-        for (int cc = 1; cc < NXC && cc < 3; ++cc) {
-          uint64_t* bar = sb(s, cc == 1 ? FB_X1 : FB_X2);
-          mbar_arrive_expect_tx(bar, 16384);
-          tma_load_3d_hint(xchunk(cc), &map_x, bar, cc * 32, 0, seq, pol_once);
-        }
-        if constexpr (C::WO_STAGE) {
-          if (mbar_wait(wo_done, pi & 1, wc)) {
-            mbar_arrive_expect_tx(sb(s, FB_X3), 16384);
-            tma_load_3d_hint(wbuf, &map_x, sb(s, FB_X3), 96, 0, seq, pol_once);
-          }
-        }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&xbar[1], NXC > 2 ? 8192 : 4096);
+        x_load(1, &xbar[1]);
+        if constexpr (NXC > 2) x_load(2, &xbar[1]);
       }
       {
         // Statistics in one pass over the shifted values r - r0 (r0 = the row's
@@ -626,20 +587,17 @@ __global__ void __launch_bounds__(512, 1)
         // the row's spread is small next to its mean.
         float shift = 0.f;
         float2 sum2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);   // packed fp32x2 partials
-        bool xok = true;
-#pragma unroll 1
-        for (int cp = 0; cp < NXC / CPR; ++cp) {   // CPR 32-column chunks per TMEM round trip
-          if (!mbar_wait_warp(sb(s, FB_X0 + CPR * cp), pi & 1, wc) ||
-              (CPR == 2 && !mbar_wait_warp(sb(s, FB_X0 + CPR * cp + 1), pi & 1, wc))) {
-            xok = false;
-            break;
-          }
-          uint32_t r[32 * CPR];
-          tmem_ld_cols(tb + 128 + 32 * CPR * cp, r);
-          // Columns [32*HH, 32*HH + 32) of r are chunk CPR*cp + HH (HH a
-          // literal at each call, so r stays in registers).
-          auto stats_chunk = [&](const int HH) {
-            const int cc = CPR * cp + HH;
+        // Chunks cc0 .. cc0 + NCH - 1 from one TMEM round trip; r = x + (acc +
+        // bo) goes back to TMEM for the second pass. NCH is 1, or 2 where
+        // registers allow (the masked variant keeps 1).
+        auto stats = [&](auto nch, int cc0) {
+          constexpr int NCH = decltype(nch)::value;
+          uint32_t r[32 * NCH];
+          if constexpr (NCH == 2) tmem_ld64(tb + 128 + 32 * cc0, r);
+          else tmem_ld32(tb + 128 + 32 * cc0, r);
+#pragma unroll
+          for (int HH = 0; HH < NCH; ++HH) {
+            const int cc = cc0 + HH;
             const uint8_t* src = xchunk(cc);
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
@@ -666,75 +624,78 @@ __global__ void __launch_bounds__(512, 1)
               r[i0 + 2] = __float_as_uint(a23.x);
               r[i0 + 3] = __float_as_uint(a23.y);
             }
-          };
-          stats_chunk(0);
-          if constexpr (CPR == 2) stats_chunk(1);
-          tmem_st_cols(tb + 128 + 32 * CPR * cp, r);
+          }
+          if constexpr (NCH == 2) tmem_st64(tb + 128 + 32 * cc0, r);
+          else tmem_st32(tb + 128 + 32 * cc0, r);
+        };
+        using One = std::integral_constant<int, 1>;
+        using Two = std::integral_constant<int, KMASK ? 1 : 2>;
+        if (!mbar_wait_warp(&xbar[0], pi & 1, wc)) break;
+        stats(One{}, 0);
+        if constexpr (NXC > 2) {   // chunk 0 consumed: chunk 3 into the k buffer
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&xbar[2], 4096);
+            x_load(3, &xbar[2]);
+          }
         }
-        // Each thread reads and later overwrites only its own row of each
-        // staging buffer, so no barrier is needed between the two passes.
-        if (!__all_sync(0xffffffffu, xok)) break;
+        if (!mbar_wait_warp(&xbar[1], pi & 1, wc)) break;
+        if constexpr (NXC > 2) {
+          stats(Two{}, 1);
+          if constexpr (KMASK) stats(One{}, 2);
+          if (!mbar_wait_warp(&xbar[2], pi & 1, wc)) break;
+          stats(One{}, 3);
+        } else {
+          stats(One{}, 1);
+        }
         const float dmean = (sum2.x + sum2.y) * inv_d;
         const float mean = shift + dmean;
         const float rstd = rsqrtf(fmaxf((sq2.x + sq2.y) * inv_d - dmean * dmean, 0.f) + a.eps2);
         // y = (r - mean) * rstd * w + b as (r * rstd - mean * rstd) * w + b, in pairs.
         const float2 rs2 = make_float2(rstd, rstd), nm2 = make_float2(-mean * rstd, -mean * rstd);
-        // y leaves in 32-column fp32 atoms (16 KB, 128-byte swizzle) by TMA
-        // store (rows >= S are clipped), each through the buffer its x chunk
-        // came in, all in one round.
-        // Second pass: y from r (kept in TMEM by the first pass), written over
-        // this row's x in place.
-        auto write_y = [&](int cp) {   // chunks CPR*cp .. from one TMEM load
-          uint32_t r[32 * CPR];
-          tmem_ld_cols(tb + 128 + 32 * CPR * cp, r);
-          auto y_chunk = [&](const int HH) {   // HH a literal at each call: r stays in registers
-            const int cc = CPR * cp + HH;
-            const uint32_t dst = smem_u32(xchunk(cc)) + row * 128;
+        // Second pass: y from r (kept in TMEM by the first pass), staged over
+        // this row's x chunk in place and stored by the warp's lane 0 (rows
+        // past S are clipped).
+        auto y_chunk = [&](const uint32_t (&r)[32], int cc) {
+          const uint32_t dst = smem_u32(xchunk(cc)) + row * 128;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              const int col = cc * 32 + 4 * c;
-              const int i0 = 32 * HH + 4 * c;
-              const float4 wv = *reinterpret_cast<const float4*>(sprm + DM + col);
-              const float4 bb = *reinterpret_cast<const float4*>(sprm + 2 * DM + col);
-              const float2 t01 = __ffma2_rn(make_float2(__uint_as_float(r[i0 + 0]), __uint_as_float(r[i0 + 1])), rs2, nm2);
-              const float2 t23 = __ffma2_rn(make_float2(__uint_as_float(r[i0 + 2]), __uint_as_float(r[i0 + 3])), rs2, nm2);
-              const float2 y01 = __ffma2_rn(t01, make_float2(wv.x, wv.y), make_float2(bb.x, bb.y));
-              const float2 y23 = __ffma2_rn(t23, make_float2(wv.z, wv.w), make_float2(bb.z, bb.w));
-              st_shared_v4(dst + ((c ^ (row & 7)) << 4), __float_as_uint(y01.x), __float_as_uint(y01.y),
-                           __float_as_uint(y23.x), __float_as_uint(y23.y));
-            }
-          };
-          y_chunk(0);
-          if constexpr (CPR == 2) y_chunk(1);
-        };
-#pragma unroll 1
-        for (int cp = 0; cp < NXC / CPR; ++cp) write_y(cp);
-        fence_proxy_async_smem();   // generic writes before the async-proxy (TMA) reads
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sb(s, FB_Y_STAGED));
-        if (leader && mbar_wait(sb(s, FB_Y_STAGED), pi & 1, wc)) {
-          // Bulk groups in the order their buffers are needed again: chunk 3
-          // (the weight buffer, back to the ring), chunks 0-1 (the k buffer
-          // and ctx blocks 0-1: k, v(0), v(1) of the next sequence), chunk 2
-          // (ctx blocks 2-3: v(2), v(3)). The leader waits for them at the
-          // start of the next sequence and before its v(2).
-          if constexpr (C::WO_STAGE) {
-            tma_store_3d_hint(&map_y, wbuf, 96, 0, seq, pol_once);
-            bulk_commit();
+          for (int c = 0; c < 8; ++c) {
+            const int col = cc * 32 + 4 * c;
+            const float4 wv = *reinterpret_cast<const float4*>(sprm + DM + col);
+            const float4 bb = *reinterpret_cast<const float4*>(sprm + 2 * DM + col);
+            const float2 t01 = __ffma2_rn(make_float2(__uint_as_float(r[4 * c + 0]), __uint_as_float(r[4 * c + 1])), rs2, nm2);
+            const float2 t23 = __ffma2_rn(make_float2(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])), rs2, nm2);
+            const float2 y01 = __ffma2_rn(t01, make_float2(wv.x, wv.y), make_float2(bb.x, bb.y));
+            const float2 y23 = __ffma2_rn(t23, make_float2(wv.z, wv.w), make_float2(bb.z, bb.w));
+            st_shared_v4(dst + ((c ^ (row & 7)) << 4), __float_as_uint(y01.x), __float_as_uint(y01.y),
+                         __float_as_uint(y23.x), __float_as_uint(y23.y));
           }
-          tma_store_3d_hint(&map_y, xchunk(0), 0, 0, seq, pol_once);
-          tma_store_3d_hint(&map_y, xchunk(1), 32, 0, seq, pol_once);
-          bulk_commit();
-          if constexpr (NXC > 2) {
-            tma_store_3d_hint(&map_y, xchunk(2), 64, 0, seq, pol_once);
-            bulk_commit();
+        };
+        // One TMEM round trip per chunk (a 64-column r spills here). Bulk
+        // groups: [y0], [y1 y2], then y3 over y0 in the k buffer once the
+        // first group has read it.
+        uint32_t r[32];
+#pragma unroll 1
+        for (int cc = 0; cc < NXC; ++cc) {
+          if (cc == 3) {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+          }
+          tmem_ld32(tb + 128 + 32 * cc, r);
+          y_chunk(r, cc);
+          fence_proxy_async_smem();   // generic writes before the async-proxy (TMA) reads
+          __syncwarp();
+          if (lane == 0) {
+            y_store(cc);
+            if (cc != 1 || NXC == 2) bulk_commit();
           }
         }
       }
       tc_fence_before();   // TMEM reads of this sequence done before the next S MMA
     }
   }
-  if (warp == 4 || warp == 8) {
+  if (warp >= 4 && warp < 12) {   // row warps: their y stores complete before exit
     if (lane == 0) bulk_wait_all();
   }
   __syncthreads();
