@@ -1,15 +1,15 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 single transformer-layer forward (one JSON line).
 
-Metric: layer tokens/s = B*S / latency, the reference
-harness's definition (torch_transformer_benchmark.py:1906-1908).
+Metric: layer tokens/s = B*S / latency, the reference harness's
+definition (torch_transformer_benchmark.py:1906-1908).
 
-Default workload: BASELINE cfg5, the configuration ``north_star``'s target is
-stated on -- B=32, S=100000, d_model=1024, H=16 (d_h=64), x fp32 ~ N(0,1),
+Default workload: cfg5, the long-context configuration the performance
+target is stated on -- B=32, S=100000, d_model=1024, H=16 (d_h=64), x fp32 ~ N(0,1),
 seeded default nn.Linear init, LayerNorm gamma=1 beta=0, no mask,
 non-causal. One step = one layer forward over the batch (x and y 13.1 GB
 each, far larger than the 126 MB L2, so no flush is needed between steps).
-``--config cfg1..cfg4`` selects the other BASELINE shapes.
+``--config cfg1..cfg4`` selects the other benchmark shapes.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5] [--impl ours|reference]
 

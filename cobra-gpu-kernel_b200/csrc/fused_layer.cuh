@@ -1,6 +1,6 @@
 // fused_layer.cuh -- the whole layer in one persistent kernel for short
 // sequences: y = LN2(x + Attn(LN1(x)) Wo^T + bo) with d_model in {64, 128},
-// head_dim 32 and S <= 128 (BASELINE cfg1 / cfg2 shapes).
+// head_dim 32 and S <= 128 (the cfg1 / cfg2 benchmark shapes).
 //
 // One sequence (<= 128 tokens) fills the M = 128 rows of every tcgen05 tile,
 // so h, q, k, v, the scores and ctx never leave the SM: per sequence the only
@@ -10,9 +10,9 @@
 // QKV+attention kernel (_qkvattn_kernel, torch_transformer_benchmark.py:654-741)
 // carried through the out-projection and both LayerNorms.
 //
-// Two sequences are processed in lockstep, one per worker warpgroup, so the
-// tensor core alternates between them while the other one is in its
-// LayerNorm / softmax / epilogue. Per sequence slot, TMEM (256 columns):
+// Two sequences are in flight, one per sequence slot (worker warpgroup), so
+// the tensor core serves one while the other is in its LayerNorm / softmax /
+// epilogue. Per sequence slot, TMEM (256 columns):
 //   [0, 96)    q|k|v projection of one head (fp32); once read, q of the head
 //              as fp16 pairs in [0, 16) (A operand of S = q k^T, from TMEM)
 //   [96, 128)  O = P v of the head (fp32)

@@ -1,7 +1,7 @@
 """Head-sharded layer forward, one process per GPU over ``torch.distributed``.
 
 Batch sharding (``sharding.py``) leaves ranks idle when the batch has fewer
-sequences than there are ranks (BASELINE cfg1: B = 4 on 8 GPUs). The heads of
+sequences than there are ranks (the cfg1 benchmark shape: B = 4 on 8 GPUs). The heads of
 one layer are independent up to the out-projection
 (torch_transformer_benchmark.py:94-118: q, k, v and the softmax are per head),
 so they can be split instead: rank r computes LN1, the q / k / v projections

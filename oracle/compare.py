@@ -12,7 +12,7 @@ from typing import List, Tuple
 
 import torch
 
-ATOL = 2e-3   # torch_transformer_benchmark.py:1960 (argparse default), BASELINE gate
+ATOL = 2e-3   # torch_transformer_benchmark.py:1960 (argparse default), the harness gate
 RTOL = 2e-2   # :1959
 
 

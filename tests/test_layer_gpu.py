@@ -1,6 +1,6 @@
 """GPU parity tests: the sm_100a path through the C ABI against the CPU oracle.
 
-Gate (BASELINE.json, torch_transformer_benchmark.py:1959-1960): every output
+Gate (torch_transformer_benchmark.py:1959-1960): every output
 element satisfies abs_err <= 2e-3 OR rel_err <= 2e-2 against the reference
 layer (the fp32 CPU oracle, itself pinned bit-exactly to the reference).
 
@@ -212,7 +212,7 @@ def test_all_true_mask_is_accepted(pkg, cuda_ok):
     ("cfg4", 64, 1024, 128, 4),
 ])
 def test_baseline_configs_full(pkg, cuda_ok, cfg_name, B, S, d, H):
-    """BASELINE cfg3 / cfg4 at full size against the CPU fp32 oracle, 5 seeds
+    """cfg3 / cfg4 at full size against the CPU fp32 oracle, 5 seeds
     (the harness default trial count, torch_transformer_benchmark.py:1958-1961)."""
     cfg, ref, lay = make_layer(pkg, B, S, d, H, False)
     for t in range(5):
@@ -227,7 +227,7 @@ def test_baseline_configs_full(pkg, cuda_ok, cfg_name, B, S, d, H):
 
 
 def test_cfg2_full_size_sampled(pkg, cuda_ok):
-    """BASELINE cfg2 (B=10000) on the GPU; the CPU oracle checks 64 sampled sequences
+    """cfg2 (B=10000) on the GPU; the CPU oracle checks 64 sampled sequences
     (sequences are independent, torch_transformer_benchmark.py:1446-1447)."""
     B, S, d, H = 10000, 128, 128, 4
     cfg, ref, lay = make_layer(pkg, B, S, d, H, False)

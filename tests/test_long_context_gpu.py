@@ -1,8 +1,7 @@
-"""BASELINE cfg5 family on the GPU: S = 100000, d = 1024, H = 16 (dh = 64).
+"""The cfg5 benchmark family on the GPU: S = 100000, d = 1024, H = 16 (dh = 64).
 
 The reference cannot run this shape (its [B,H,S,S] scores would be 19,073 GiB,
-torch_transformer_benchmark.py:98), so correctness is checked as BASELINE.json
-prescribes: a seeded subset of 256 query positions per sequence against an fp64
+torch_transformer_benchmark.py:98), so correctness is checked on sampled rows: a seeded subset of 256 query positions per sequence against an fp64
 CPU oracle that streams over all keys (oracle.streamed_layer_rows_fp64, a
 restatement of tools/reference_chunked.py:73-128). The full cfg5 batch of 32
 sequences runs in one launch (the launch the benchmark times: 32 x 16 x 391

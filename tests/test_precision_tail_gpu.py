@@ -4,7 +4,7 @@ The reference's own campaign (tools/precision_probe.py:23-58, reported in
 report/TECH_REPORT.md:515-522) runs its optimized model against
 BaselineTransformer over seeds 1000+t, input scales 0.5 / 1 / 2 and padding
 ratios 0 / 0.3, and reports the worst max_abs error with its margin to the
-gate (atol / worst). This test does the same for BASELINE cfg1-cfg4 with the
+gate (atol / worst). This test does the same for cfg1-cfg4 with the
 CPU fp32 oracle (pinned bit-exactly to the reference): 20 seeds x 3 scales x 2
 paddings = 120 cases per config, every output element under the reference's
 gate ``abs <= 2e-3 OR rel <= 2e-2``. cfg2's 10000 sequences are represented

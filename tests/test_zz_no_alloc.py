@@ -15,7 +15,7 @@ library's scratch (``b200l_noalloc_read_status``), which is where a kernel
 of a no-alloc call records a device-side failure. It also checks that a
 problem too large for the built-in scratch is refused with a clear error
 instead of running. The whole-layer kernel (d_model 128, head_dim 32,
-S <= 128) needs only the status block, so the full BASELINE cfg2 batch
+S <= 128) needs only the status block, so the full cfg2 batch
 (10000 sequences) runs through the no-alloc entry point too.
 
 This file is named so that pytest collects it last.
