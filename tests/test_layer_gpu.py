@@ -260,6 +260,8 @@ FUSED_SHAPES = [
     (1, 1, 128, 4, False),      # S = 1
     (2, 100, 64, 2, False),     # d = 64
     (300, 128, 128, 4, False),  # more pairs than SMs: persistent loop
+    (301, 128, 128, 4, False),  # odd batch over more pairs than SMs: slot 1 idle in the last pair
+    (299, 100, 64, 2, True),    # the same at d = 64, S < 128, causal
 ]
 
 
